@@ -1,0 +1,451 @@
+"""Benchmark of the b200k kernels on the op suite's named configurations.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl b200k|reference]
+
+One JSON line on stdout (rank 0).  Metric: achieved HBM GB/s of the op
+(algorithmic bytes: compulsory reads + writes, per step) aggregated over all
+ranks, with the % of the measured HBM peak in `roofline`.
+
+Workloads (synthetic data of the named shapes, seeded per rank):
+  chain     (default) residual add -> LayerNorm -> GELU-tanh, bf16,
+            x, r [16384, 8192], outputs (h = x + r, y), eps 1e-5
+  rmsnorm   x [4096, 4096] fp16, w = 1 + 0.1 N(0,1), eps 1e-6
+  swiglu    gate, up [8192, 14336] bf16, N(0,1)*2
+  rope      q [8,4096,32,128], k [8,4096,8,128] bf16, tables [4096, 64]
+  rope_interleaved   same shapes, GPT-J pairs
+  ce        logits [32768, 128256] bf16, N(0,1)*3, 5% targets = -100,
+            mean loss over valid rows (rows split across ranks, NCCL
+            all-reduce of [loss sum, valid count])
+Each rank processes a full configuration (weak scaling) except `ce`, whose
+32768 rows are split across ranks (strong scaling).
+
+--impl reference times the CPU implementation of the same workload (the
+oracle's numpy restatement of ouroboros/specs.py, all host cores) on a bounded
+sample of rows per step, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ouroboros-kernelsmith_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------
+# peaks / clocks
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            v = float(json.load(f)["hbm_gbs"])
+        return v, "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index, period=0.002):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.period = period
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "n_samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "n_samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+def _randn(shape, dtype, device, seed, scale=1.0, shift=0.0):
+    g = torch.Generator(device=device).manual_seed(seed)
+    return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * scale
+            + shift).to(dtype)
+
+
+class Workload:
+    name = ""
+    scaling = "weak"
+    dtype = "bf16"
+    launches_per_step = 1
+
+    def setup(self, device, rank, world): ...
+    def step(self): ...
+    def bytes_per_step(self) -> int: ...
+    def config(self) -> dict: ...
+    def e2e_setup(self): ...
+    def e2e_step(self, timing): ...
+    def cpu_rows(self) -> int: ...
+    def cpu_run(self, r0, r1): ...
+
+
+class Chain(Workload):
+    """x + r -> LayerNorm -> GELU-tanh, outputs (h, y); configs[1] shape."""
+    name = "chain_add_layernorm_gelu"
+    M, N = 16384, 8192
+
+    def setup(self, device, rank, world):
+        import b200k
+        self.b2k = b200k
+        s = 1000 * rank
+        self.x = _randn((self.M, self.N), torch.bfloat16, device, s + 1)
+        self.r = _randn((self.M, self.N), torch.bfloat16, device, s + 2)
+        self.w = _randn((self.N,), torch.bfloat16, device, s + 3, 0.1, 1.0)
+        self.b = _randn((self.N,), torch.bfloat16, device, s + 4, 0.02)
+        self.device = device
+
+    def step(self):
+        return self.b2k.fused_add_norm(self.x, self.r, self.w, self.b, norm="layer", act="gelu")
+
+    def bytes_per_step(self):
+        # read x, r; write h, y (bf16); read gamma, beta
+        return 4 * self.M * self.N * 2 + 2 * self.N * 2
+
+    def config(self):
+        return {"workload": "add_layernorm_gelu_tanh_h_y", "M": self.M, "N": self.N,
+                "outputs": "h=x+r, y=gelu_tanh(LN(h)*g+b)", "eps": 1e-5,
+                "l2": "inputs exceed L2 (1 GiB working set per step)"}
+
+    def e2e_setup(self):
+        self.hx = self.x.cpu().pin_memory()
+        self.hr = self.r.cpu().pin_memory()
+        self.hw = self.w.cpu()
+        self.hb = self.b.cpu()
+        self.hh = torch.empty_like(self.hx).pin_memory()
+        self.hy = torch.empty_like(self.hx).pin_memory()
+        return (2 * self.M * self.N * 2 + 2 * self.N * 2, 2 * self.M * self.N * 2)
+
+    def e2e_step(self, timing):
+        from b200k.host import run_rows_host
+        b2k = self.b2k
+        run_rows_host(lambda x, r, w, b: b2k.fused_add_norm(x, r, w, b, norm="layer", act="gelu"),
+                      [self.hx, self.hr], [self.hw, self.hb], out=(self.hh, self.hy),
+                      device=self.device, timing=timing)
+
+    # CPU: oracle restatement of the same chain on float32 values
+    def cpu_prepare(self):
+        from oracle.numerics import bf16_round
+        rows = self.cpu_rows_total = min(self.M, 4096)
+        g = np.random.default_rng(0)
+        self.cx = bf16_round(g.standard_normal((rows, self.N), dtype=np.float32))
+        self.cr = bf16_round(g.standard_normal((rows, self.N), dtype=np.float32))
+        self.cw = bf16_round(1 + 0.1 * g.standard_normal(self.N, dtype=np.float32))
+        self.cb = bf16_round(0.02 * g.standard_normal(self.N, dtype=np.float32))
+
+    def cpu_run(self, r0, r1):
+        from oracle import ops as O
+        from oracle.numerics import rnd
+        h = rnd(self.cx[r0:r1] + self.cr[r0:r1], "bf16")
+        y = O.chain("layer", True, "gelu", [self.cx[r0:r1], self.cr[r0:r1], self.cw, self.cb],
+                    "bf16")
+        return h, y
+
+    def cpu_bytes_per_row(self):
+        return 4 * self.N * 2
+
+
+class RMSNorm(Workload):
+    """rmsnorm x [4096, 4096] fp16; buffers rotate over 8 sets."""
+    name = "rmsnorm"
+    dtype = "fp16"
+    M = N = 4096
+    SETS = 8
+
+    def setup(self, device, rank, world):
+        import b200k
+        self.b2k = b200k
+        s = 1000 * rank
+        self.xs = [_randn((self.M, self.N), torch.float16, device, s + 10 + i) for i in range(self.SETS)]
+        self.w = _randn((self.N,), torch.float16, device, s + 3, 0.1, 1.0)
+        self.i = 0
+        self.device = device
+
+    def step(self):
+        x = self.xs[self.i % self.SETS]
+        self.i += 1
+        return self.b2k.rmsnorm(x, self.w)
+
+    def bytes_per_step(self):
+        return 2 * self.M * self.N * 2 + self.N * 2
+
+    def config(self):
+        return {"workload": "rmsnorm", "M": self.M, "N": self.N, "eps": 1e-6,
+                "l2": f"{self.SETS} rotating input sets ({self.SETS * self.M * self.N * 2 >> 20} MiB) "
+                      "so consecutive steps read cold data"}
+
+    def e2e_setup(self):
+        self.hx = self.xs[0].cpu().pin_memory()
+        self.hw = self.w.cpu()
+        self.hy = torch.empty_like(self.hx).pin_memory()
+        return (self.M * self.N * 2 + self.N * 2, self.M * self.N * 2)
+
+    def e2e_step(self, timing):
+        from b200k.host import run_rows_host
+        run_rows_host(self.b2k.rmsnorm, [self.hx], [self.hw], out=self.hy, device=self.device,
+                      timing=timing)
+
+    def cpu_prepare(self):
+        from oracle.numerics import f16_round
+        g = np.random.default_rng(0)
+        self.cx = f16_round(g.standard_normal((self.M, self.N), dtype=np.float32))
+        self.cw = f16_round(1 + 0.1 * g.standard_normal(self.N, dtype=np.float32))
+        self.cpu_rows_total = self.M
+
+    def cpu_run(self, r0, r1):
+        from oracle import ops as O
+        return O.rmsnorm(self.cx[r0:r1], self.cw, "f16")
+
+    def cpu_bytes_per_row(self):
+        return 2 * self.N * 2
+
+
+WORKLOADS = {"chain": Chain, "rmsnorm": RMSNorm}
+
+
+# ---------------------------------------------------------------------------
+# CPU timing (oracle on the host cores)
+def cpu_measure(wl, budget_s=10.0, threads=None, rows_per_task=64):
+    """Runs the oracle over row chunks on `threads` host threads for about
+    budget_s seconds; returns (GB/s, threads, rows processed, seconds)."""
+    from concurrent.futures import ThreadPoolExecutor
+    threads = threads or os.cpu_count() or 1
+    wl.cpu_prepare()
+    total = wl.cpu_rows_total
+    rows_per_task = max(1, min(rows_per_task, total))
+    done_rows = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        while True:
+            futs = []
+            for i in range(threads):
+                r0 = (i * rows_per_task) % max(1, total - rows_per_task + 1)
+                futs.append(ex.submit(wl.cpu_run, r0, r0 + rows_per_task))
+            for f in futs:
+                f.result()
+            done_rows += threads * rows_per_task
+            el = time.perf_counter() - t0
+            if el >= budget_s:
+                break
+    gbs = done_rows * wl.cpu_bytes_per_row() / el / 1e9
+    return gbs, threads, done_rows, el
+
+
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", default="chain", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="b200k", choices=["b200k", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    wl = WORKLOADS[args.workload]()
+
+    if args.impl == "reference":
+        return run_reference(args, wl, rank, world)
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    wl.setup(device, rank, world)
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            wl.step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = ms
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+
+    total_bytes = wl.bytes_per_step() * (world if wl.scaling == "weak" else 1)
+    value = total_bytes / (ms_max * 1e-3) / 1e9
+    peak, peak_kind = hbm_peak()
+    per_launch_ms = ms / wl.launches_per_step
+    achieved = wl.bytes_per_step() / wl.launches_per_step / (per_launch_ms * 1e-3) / 1e9
+
+    # end to end through the host-buffer API (pinned host in, pinned host out)
+    e2e = None
+    if not args.no_e2e:
+        h2d, d2h = wl.e2e_setup()
+        times = []
+        for i in range(3 + max(3, min(args.steps, 10))):
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            barrier()
+            wl.e2e_step(ev)
+            if i >= 3:
+                times.append(ev[0].elapsed_time(ev[1]))
+        e_ms = statistics.median(times)
+        if dist is not None:
+            t = torch.tensor([e_ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": round(total_bytes / (e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+               "ms_per_step": round(e_ms, 4), "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "api": "b200k.host.run_rows_host (pinned host buffers)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        gbs, threads, rows, el = cpu_measure(wl, args.cpu_budget)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"{rows} rows of the same workload in {el:.1f} s (numpy oracle, "
+                         f"{threads} threads)"}
+
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        try:
+            with open(tp) as f:
+                traffic = json.load(f).get(wl.name)
+        except Exception:
+            traffic = None
+
+    line = {
+        "metric": "achieved HBM GB/s (algorithmic bytes / step time), aggregate over GPUs",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True,
+        "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+        "config": dict(wl.config(), parallelism=f"rows x{world}" if world > 1 else "1 GPU"),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_source": peak_kind,
+                     "algorithmic_bytes_per_launch": wl.bytes_per_step() // wl.launches_per_step},
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+        "gpu_launches": args.steps * wl.launches_per_step,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_reference(args, wl, rank, world):
+    """CPU implementation of the same workload (oracle port, all host threads)."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    wl.cpu_prepare()
+    from concurrent.futures import ThreadPoolExecutor
+    rows_per_task = 32
+    per_step_rows = threads * rows_per_task
+    total = wl.cpu_rows_total
+    times = []
+    with ThreadPoolExecutor(threads) as ex:
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            futs = [ex.submit(wl.cpu_run, (k * rows_per_task) % max(1, total - rows_per_task + 1),
+                              (k * rows_per_task) % max(1, total - rows_per_task + 1) + rows_per_task)
+                    for k in range(threads)]
+            for f in futs:
+                f.result()
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+    s = statistics.median(times)
+    gbs = per_step_rows * wl.cpu_bytes_per_row() / s / 1e9
+    line = {
+        "impl": "reference",
+        "metric": "achieved HBM GB/s (algorithmic bytes / step time), aggregate over GPUs",
+        "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(s * 1e3, 3), "higher_is_better": True,
+        "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+        "config": wl.config(),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{per_step_rows} rows per step (numpy restatement of "
+                                   "ouroboros/specs.py, one row chunk per thread)"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

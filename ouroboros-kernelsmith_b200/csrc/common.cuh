@@ -1,0 +1,321 @@
+// Shared device helpers for the b200k kernels: element traits, 16-byte vector
+// load/store with cache hints, group reductions and the epilogue functions of
+// the chain grammar (ouroboros/chains.py:13-53).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <math.h>
+#include <type_traits>
+
+#include "b200k.h"
+
+namespace b2k {
+
+constexpr float kLog2e = 1.4426950408889634f;   // log2(e)
+constexpr float kLn2 = 0.6931471805599453f;     // ln(2)
+constexpr float kGeluC = 0.7978845608028654f;   // sqrt(2/pi), chains.py:10
+
+// ---------------------------------------------------------------------------
+// element traits: E = elements per 16-byte vector
+template <typename T> struct Traits;
+template <> struct Traits<float> { static constexpr int E = 4; };
+template <> struct Traits<__half> { static constexpr int E = 8; };
+template <> struct Traits<__nv_bfloat16> { static constexpr int E = 8; };
+
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// value after a round trip through T (models a `.to(dtype)` in the reference)
+template <typename T> __device__ __forceinline__ float round_to(float v) {
+  return to_f<T>(from_f<T>(v));
+}
+
+// 16-byte vector -> E floats
+template <typename T> __device__ __forceinline__ void unpack(const uint4& v, float* f);
+template <> __device__ __forceinline__ void unpack<float>(const uint4& v, float* f) {
+  f[0] = __uint_as_float(v.x); f[1] = __uint_as_float(v.y);
+  f[2] = __uint_as_float(v.z); f[3] = __uint_as_float(v.w);
+}
+template <> __device__ __forceinline__ void unpack<__nv_bfloat16>(const uint4& v, float* f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+template <> __device__ __forceinline__ void unpack<__half>(const uint4& v, float* f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h2 = *reinterpret_cast<const __half2*>(&w[i]);
+    float2 t = __half22float2(h2);
+    f[2 * i] = t.x; f[2 * i + 1] = t.y;
+  }
+}
+
+// E floats -> 16-byte vector (round to nearest even)
+template <typename T> __device__ __forceinline__ uint4 pack(const float* f);
+template <> __device__ __forceinline__ uint4 pack<float>(const float* f) {
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                    __float_as_uint(f[3]));
+}
+template <> __device__ __forceinline__ uint4 pack<__nv_bfloat16>(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 p = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&p);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <> __device__ __forceinline__ uint4 pack<__half>(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 p = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&p);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// ---------------------------------------------------------------------------
+// global memory access.  Streaming operands (read or written once) use the
+// evict-first (.cs) forms so they do not push reused data (weights, tables,
+// rows re-read in a later pass) out of L2.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ uint4 ld_keep(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ void st_stream(void* p, const uint4& v) {
+  __stcs(reinterpret_cast<uint4*>(p), v);
+}
+__device__ __forceinline__ uint4 zero4() { return make_uint4(0u, 0u, 0u, 0u); }
+
+template <typename T> __device__ __forceinline__ float ld1(const T* p) { return to_f<T>(p[0]); }
+template <typename T> __device__ __forceinline__ void st1(T* p, float v) { p[0] = from_f<T>(v); }
+
+// ---------------------------------------------------------------------------
+// PTX approximations (hardware MUFU ops), used only where the output is a
+// 16-bit float: their relative error (<= ~2^-21 for ex2/rcp/lg2, ~2^-11 for
+// tanh) is below half an fp16 ulp after the final rounding.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y; asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x)); return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y; asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x)); return y;
+}
+__device__ __forceinline__ float lg2_approx(float x) {
+  float y; asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x)); return y;
+}
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y; asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x)); return y;
+}
+
+// exp / log / sigmoid / tanh in two precisions.  P (precise) = fp32 output,
+// library functions; !P = 16-bit output, MUFU forms.
+template <bool P> __device__ __forceinline__ float f_exp(float x) {
+  if constexpr (P) return expf(x); else return ex2_approx(x * kLog2e);
+}
+template <bool P> __device__ __forceinline__ float f_log(float x) {
+  if constexpr (P) return logf(x); else return lg2_approx(x) * kLn2;
+}
+template <bool P> __device__ __forceinline__ float f_rcp(float x) {
+  if constexpr (P) return 1.0f / x; else return rcp_approx(x);
+}
+template <bool P> __device__ __forceinline__ float f_sigmoid(float x) {
+  return f_rcp<P>(1.0f + f_exp<P>(-x));
+}
+// tanh with an ABSOLUTE error of ~1e-7 everywhere (1 - 2/(e^{2x}+1)); used
+// where the tanh feeds an exp (softcap), unlike tanh.approx whose relative
+// error would be amplified by the cap.
+template <bool P> __device__ __forceinline__ float f_tanh_abs(float x) {
+  if constexpr (P) return tanhf(x);
+  else return 1.0f - 2.0f * rcp_approx(ex2_approx(2.0f * kLog2e * x) + 1.0f);
+}
+template <bool P> __device__ __forceinline__ float f_tanh(float x) {
+  if constexpr (P) return tanhf(x); else return tanh_approx(x);
+}
+
+// ---------------------------------------------------------------------------
+// Epilogues, chains.py:13-53.  The gelu/tanh identity 0.5*(1+tanh(u)) =
+// sigmoid(2u) is used in the MUFU form (no cancellation for large negative
+// inputs); the precise form is the reference formula itself.
+template <int ACT, bool P> __device__ __forceinline__ float act_apply(float t) {
+  if constexpr (ACT == B2K_ACT_NONE) {
+    return t;
+  } else if constexpr (ACT == B2K_ACT_GELU) {
+    const float u = kGeluC * (t + 0.044715f * t * t * t);
+    if constexpr (P) return 0.5f * t * (1.0f + tanhf(u));
+    else return t * f_sigmoid<false>(2.0f * u);
+  } else if constexpr (ACT == B2K_ACT_SILU) {
+    return t * f_sigmoid<P>(t);
+  } else if constexpr (ACT == B2K_ACT_RELU2) {
+    const float r = fmaxf(t, 0.0f); return r * r;
+  } else if constexpr (ACT == B2K_ACT_TANH) {
+    return f_tanh<P>(t);
+  } else if constexpr (ACT == B2K_ACT_SIGMOID) {
+    return f_sigmoid<P>(t);
+  } else if constexpr (ACT == B2K_ACT_RELU) {
+    return fmaxf(t, 0.0f);
+  } else if constexpr (ACT == B2K_ACT_SQUARE) {
+    return t * t;
+  } else if constexpr (ACT == B2K_ACT_ABS) {
+    return fabsf(t);
+  } else if constexpr (ACT == B2K_ACT_SOFTSIGN) {
+    if constexpr (P) return t / (1.0f + fabsf(t));
+    else return t * rcp_approx(1.0f + fabsf(t));
+  } else if constexpr (ACT == B2K_ACT_HARDSIGMOID) {
+    const float c = fminf(fmaxf(t + 3.0f, 0.0f), 6.0f);
+    if constexpr (P) return c / 6.0f; else return c * (1.0f / 6.0f);
+  } else if constexpr (ACT == B2K_ACT_HARDSWISH) {
+    const float c = t * fminf(fmaxf(t + 3.0f, 0.0f), 6.0f);
+    if constexpr (P) return c / 6.0f; else return c * (1.0f / 6.0f);
+  } else if constexpr (ACT == B2K_ACT_LEAKY_RELU) {
+    return t > 0.0f ? t : 0.01f * t;
+  } else if constexpr (ACT == B2K_ACT_RELU6) {
+    return fminf(fmaxf(t, 0.0f), 6.0f);
+  } else if constexpr (ACT == B2K_ACT_HARDTANH) {
+    return fminf(fmaxf(t, -1.0f), 1.0f);
+  } else if constexpr (ACT == B2K_ACT_ELU) {
+    return t > 0.0f ? t : f_exp<P>(fminf(t, 0.0f)) - 1.0f;
+  } else if constexpr (ACT == B2K_ACT_SELU) {
+    return 1.0507009873554805f *
+           (t > 0.0f ? t : 1.6732632423543772f * (f_exp<P>(fminf(t, 0.0f)) - 1.0f));
+  } else if constexpr (ACT == B2K_ACT_SOFTPLUS) {
+    return t > 20.0f ? t : f_log<P>(1.0f + f_exp<P>(fminf(t, 20.0f)));
+  } else if constexpr (ACT == B2K_ACT_MISH) {
+    const float sp = t > 20.0f ? t : f_log<P>(1.0f + f_exp<P>(fminf(t, 20.0f)));
+    return t * f_tanh<P>(sp);
+  } else if constexpr (ACT == B2K_ACT_GELU_ERF) {
+    return 0.5f * t * (1.0f + erff(t * 0.7071067811865476f));
+  } else {
+    static_assert(ACT >= 0 && ACT < B2K_ACT_COUNT, "unknown epilogue");
+    return t;
+  }
+}
+
+// Expands F(std::integral_constant<int, ACT>) for a runtime `act` value.
+template <typename F> __device__ __forceinline__ void dispatch_act(int act, F&& f) {
+#define B2K_ACT_CASE(k) case k: f(std::integral_constant<int, k>{}); break;
+  switch (act) {
+    B2K_ACT_CASE(0) B2K_ACT_CASE(1) B2K_ACT_CASE(2) B2K_ACT_CASE(3) B2K_ACT_CASE(4)
+    B2K_ACT_CASE(5) B2K_ACT_CASE(6) B2K_ACT_CASE(7) B2K_ACT_CASE(8) B2K_ACT_CASE(9)
+    B2K_ACT_CASE(10) B2K_ACT_CASE(11) B2K_ACT_CASE(12) B2K_ACT_CASE(13) B2K_ACT_CASE(14)
+    B2K_ACT_CASE(15) B2K_ACT_CASE(16) B2K_ACT_CASE(17) B2K_ACT_CASE(18) B2K_ACT_CASE(19)
+    default: break;
+  }
+#undef B2K_ACT_CASE
+}
+
+// ---------------------------------------------------------------------------
+// Group reductions.  A thread block is (G, R): G threads (threadIdx.x) share
+// one row, R rows (threadIdx.y) per block, G*R a multiple of 32, G a power of
+// two.  Every thread of the block must call these (they may __syncthreads).
+// `red` is shared scratch of 1024 floats.  The result is returned to
+// every thread of the group, summed in a fixed order (deterministic).
+struct Group {
+  int G, tx, ty;
+  __device__ __forceinline__ Group() : G(blockDim.x), tx(threadIdx.x), ty(threadIdx.y) {}
+};
+
+template <typename Op>
+__device__ __forceinline__ float group_reduce(float v, const Group& g, float* red, Op op) {
+  const int width = g.G < 32 ? g.G : 32;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    if (o < width) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (g.G > 32) {
+    const int nw = g.G >> 5;
+    if ((g.tx & 31) == 0) red[g.ty * 32 + (g.tx >> 5)] = v;
+    __syncthreads();
+    float t = red[g.ty * 32];
+    for (int i = 1; i < nw; ++i) t = op(t, red[g.ty * 32 + i]);
+    __syncthreads();
+    v = t;
+  }
+  return v;
+}
+
+struct OpSum { __device__ __forceinline__ float operator()(float a, float b) const { return a + b; } };
+struct OpMax { __device__ __forceinline__ float operator()(float a, float b) const { return fmaxf(a, b); } };
+
+__device__ __forceinline__ float group_sum(float v, const Group& g, float* red) {
+  return group_reduce(v, g, red, OpSum{});
+}
+__device__ __forceinline__ float group_max(float v, const Group& g, float* red) {
+  return group_reduce(v, g, red, OpMax{});
+}
+
+// (max, sum-of-exp) pair merge for online logsumexp.  s is relative to m.
+__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
+  const float M = fmaxf(m, m2);
+  if (M == -INFINITY) return;  // both empty
+  s = s * ex2_approx((m - M) * kLog2e) + s2 * ex2_approx((m2 - M) * kLog2e);
+  m = M;
+}
+
+__device__ __forceinline__ void group_lse(float& m, float& s, const Group& g, float* red) {
+  const int width = g.G < 32 ? g.G : 32;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    if (o < width) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      lse_merge(m, s, m2, s2);
+    }
+  if (g.G > 32) {
+    const int nw = g.G >> 5;
+    float* rm = red;        // [R][32], R <= 16 when G > 32
+    float* rs = red + 512;  // [R][32]  (red must hold 1024 floats)
+    if ((g.tx & 31) == 0) { rm[g.ty * 32 + (g.tx >> 5)] = m; rs[g.ty * 32 + (g.tx >> 5)] = s; }
+    __syncthreads();
+    float M = rm[g.ty * 32], S = rs[g.ty * 32];
+    for (int i = 1; i < nw; ++i) lse_merge(M, S, rm[g.ty * 32 + i], rs[g.ty * 32 + i]);
+    __syncthreads();
+    m = M; s = S;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side helpers (defined in api.cu)
+void set_error(const char* fmt, ...);
+int sm_count();
+int check_launch(const char* what);
+bool aligned16(const void* p);
+int dtype_size(int dtype);
+
+}  // namespace b2k
+
+#define B2K_REQUIRE(cond, ...)                 \
+  do {                                         \
+    if (!(cond)) {                             \
+      ::b2k::set_error(__VA_ARGS__);           \
+      return B2K_EINVAL;                       \
+    }                                          \
+  } while (0)
+
+// Runs BODY with `T` bound to the element type of a floating dtype.
+#define B2K_DISPATCH_FLOAT(dtype, ...)                                          \
+  switch (dtype) {                                                              \
+    case B2K_F32: { using T = float; __VA_ARGS__; break; }                      \
+    case B2K_F16: { using T = __half; __VA_ARGS__; break; }                     \
+    case B2K_BF16: { using T = __nv_bfloat16; __VA_ARGS__; break; }             \
+    default: ::b2k::set_error("unsupported dtype %d", (int)(dtype)); return B2K_EINVAL; \
+  }
