@@ -256,7 +256,56 @@ class RMSNorm(Workload):
         return 2 * self.N * 2
 
 
-WORKLOADS = {"chain": Chain, "rmsnorm": RMSNorm}
+class SwiGLU(Workload):
+    """configs[2]: silu(gate) * up, gate/up [8192, 14336] bf16, N(0,1)*2."""
+    name = "swiglu"
+    M, N = 8192, 14336
+
+    def setup(self, device, rank, world):
+        import b200k
+        self.b2k = b200k
+        s = 1000 * rank
+        self.g = _randn((self.M, self.N), torch.bfloat16, device, s + 21, 2.0)
+        self.u = _randn((self.M, self.N), torch.bfloat16, device, s + 22, 2.0)
+        self.device = device
+
+    def step(self):
+        return self.b2k.swiglu(self.g, self.u)
+
+    def bytes_per_step(self):
+        return 3 * self.M * self.N * 2
+
+    def config(self):
+        return {"workload": "swiglu", "M": self.M, "N": self.N,
+                "l2": "inputs exceed L2 (470 MB read per step)"}
+
+    def e2e_setup(self):
+        self.hg = self.g.cpu().pin_memory()
+        self.hu = self.u.cpu().pin_memory()
+        self.hy = torch.empty_like(self.hg).pin_memory()
+        return (2 * self.M * self.N * 2, self.M * self.N * 2)
+
+    def e2e_step(self, timing):
+        from b200k.host import run_rows_host
+        run_rows_host(self.b2k.swiglu, [self.hg, self.hu], [], out=self.hy, device=self.device,
+                      timing=timing)
+
+    def cpu_prepare(self):
+        from oracle.numerics import bf16_round
+        g = np.random.default_rng(0)
+        rows = self.cpu_rows_total = 1024
+        self.cg = bf16_round(2 * g.standard_normal((rows, self.N), dtype=np.float32))
+        self.cu = bf16_round(2 * g.standard_normal((rows, self.N), dtype=np.float32))
+
+    def cpu_run(self, r0, r1):
+        from oracle import ops as O
+        return O.swiglu(self.cg[r0:r1], self.cu[r0:r1], "bf16")
+
+    def cpu_bytes_per_row(self):
+        return 3 * self.N * 2
+
+
+WORKLOADS = {"chain": Chain, "rmsnorm": RMSNorm, "swiglu": SwiGLU}
 
 
 # ---------------------------------------------------------------------------

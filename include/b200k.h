@@ -83,6 +83,13 @@ int b2k_version(void);
 /* Message of the last failed call on this host thread ("" if none). */
 const char* b2k_last_error(void);
 
+/* Number of bounded pipeline waits that gave up (each is a failed kernel
+ * whose outputs are incomplete) since the last reset, summed over all kernel
+ * families; reset != 0 clears the counters.  Synchronous: call after the
+ * work of interest has completed.  No reference counterpart (the Triton
+ * kernels have no device-side waits). */
+unsigned b2k_pipeline_timeouts(int reset);
+
 /* Residual -> {RMSNorm, L2, LayerNorm} -> affine -> epilogue, one row per
  * thread group, row held in registers (rows longer than the register budget
  * stream through L2 in two or three passes).

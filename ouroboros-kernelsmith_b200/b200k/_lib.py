@@ -30,6 +30,7 @@ ACT = {name: i for i, name in enumerate(ACT_NAMES)}
 SIGNATURES = {
     "b2k_version": (c_int, []),
     "b2k_last_error": (ctypes.c_char_p, []),
+    "b2k_pipeline_timeouts": (ctypes.c_uint, [c_int]),
     "b2k_norm": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                          c_int64, c_void_p, c_int64, c_int64, c_int64, c_int, c_int, c_int, c_int,
                          c_float, c_void_p]),

@@ -3,6 +3,7 @@
 #include <stdio.h>
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace b2k {
 
@@ -41,6 +42,13 @@ int check_launch(const char* what) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+static TimeoutReader g_readers[64];
+static int g_nreaders = 0;
+
+void register_timeout_reader(TimeoutReader f) {
+  if (g_nreaders < 64) g_readers[g_nreaders++] = f;
+}
+
 int dtype_size(int dtype) {
   switch (dtype) {
     case B2K_F32: return 4;
@@ -57,3 +65,9 @@ int dtype_size(int dtype) {
 extern "C" int b2k_version(void) { return 100; }  // 0.1.0
 
 extern "C" const char* b2k_last_error(void) { return b2k::g_err; }
+
+extern "C" unsigned b2k_pipeline_timeouts(int reset) {
+  unsigned total = 0;
+  for (int i = 0; i < b2k::g_nreaders; ++i) total += b2k::g_readers[i](reset != 0);
+  return total;
+}

@@ -319,3 +319,45 @@ int dtype_size(int dtype);
     case B2K_BF16: { using T = __nv_bfloat16; __VA_ARGS__; break; }             \
     default: ::b2k::set_error("unsupported dtype %d", (int)(dtype)); return B2K_EINVAL; \
   }
+
+// ---------------------------------------------------------------------------
+// Packed fp32 pairs (sm_100 f32x2 FMA/ADD/MUL: one instruction per pair).
+namespace b2k {
+
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 f2s(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
+// E floats <-> E/2 pairs views of a 16-byte vector
+template <typename T> __device__ __forceinline__ void unpack2(const uint4& v, float2* f) {
+  unpack<T>(v, reinterpret_cast<float*>(f));
+}
+template <typename T> __device__ __forceinline__ uint4 pack2(const float2* f) {
+  return pack<T>(reinterpret_cast<const float*>(f));
+}
+
+// Pairwise epilogue.  Transcendental-free epilogues and the precise (fp32
+// output) forms apply the scalar act_apply per lane; the MUFU forms of the
+// sigmoid-based epilogues do their polynomial/affine parts as f32x2 ops.
+template <int ACT, bool P> __device__ __forceinline__ float2 act_apply2(float2 t) {
+  if constexpr (!P && ACT == B2K_ACT_GELU) {
+    // x * sigmoid(2u), 2u = 2*sqrt(2/pi)*(x + 0.044715 x^3); z = -2u*log2(e)
+    constexpr float k0 = -2.0f * kGeluC * kLog2e;
+    constexpr float k1 = -2.0f * kGeluC * 0.044715f * kLog2e;
+    const float2 a = mul2(t, t);
+    const float2 z = mul2(t, fma2(a, f2s(k1), f2s(k0)));
+    const float2 d = add2(f2(ex2_approx(z.x), ex2_approx(z.y)), f2s(1.0f));
+    return mul2(t, f2(rcp_approx(d.x), rcp_approx(d.y)));
+  } else if constexpr (!P && (ACT == B2K_ACT_SILU || ACT == B2K_ACT_SIGMOID)) {
+    const float2 z = mul2(t, f2s(-kLog2e));
+    const float2 d = add2(f2(ex2_approx(z.x), ex2_approx(z.y)), f2s(1.0f));
+    const float2 s = f2(rcp_approx(d.x), rcp_approx(d.y));
+    return ACT == B2K_ACT_SILU ? mul2(t, s) : s;
+  } else {
+    return f2(act_apply<ACT, P>(t.x), act_apply<ACT, P>(t.y));
+  }
+}
+
+}  // namespace b2k

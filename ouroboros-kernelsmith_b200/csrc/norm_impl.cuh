@@ -3,21 +3,38 @@
 // layernorm_gelu, rmsnorm_gemma, rmsnorm_wide and the 76 chains
 // (ouroboros/specs.py:75-120,171-190,216-220; ouroboros/chains.py:69-87).
 //
-// One thread group per row.  The row is read from HBM exactly once into
-// registers (16-byte coalesced loads, evict-first), the statistics are group
-// reductions over registers (LayerNorm: two-pass mean then centred variance,
-// the reference's order), and the output is written once.  Rows longer than
-// 512 threads x 8 vector slots take the streaming kernel, which re-reads the
-// row from L2 for its later passes.
+// Two kernels:
+//  * norm_tma_kernel — aligned rows of 4..64 KB (per input).  Persistent CTAs
+//    (a few per SM) walk their rows through an S-stage shared-memory ring
+//    filled by bulk copies (cp.async.bulk, mbarrier completion): while one
+//    row is normalised, the next S-1 rows are already streaming in.  Weights
+//    live in registers for the whole kernel.  Every element is read from HBM
+//    once and written once.
+//  * norm_rows_kernel — everything else (short rows, several rows per block;
+//    odd N / misaligned views with scalar accesses), row in registers, one
+//    read, one write; rows beyond 512 threads x 4 slots stream through L2
+//    (norm_rows_stream_kernel).
 //
-// The epilogue is a template parameter (one kernel per activation) so each
-// kernel stays small; instances are spread over the norm_inst_*.cu files so
-// they compile in parallel.
+// LayerNorm statistics use per-thread two-pass moments merged across the
+// block with Chan et al.'s pairwise update (one block reduction per row);
+// the result equals the reference's mean-then-centred-variance up to fp32
+// rounding.  The (norm, affine) mode and the epilogue are template
+// parameters; instances are spread over norm_inst_*.cu.
 #pragma once
 
 #include "rowio.cuh"
+#include "tma.cuh"
 
 namespace b2k {
+
+// supported (norm, affine) combinations
+enum NormMode {
+  NM_LN = 0,        // LayerNorm, n = (h-mu)*rs*w + b        (+ any epilogue)
+  NM_RMS_W = 1,     // n = h*rs*w                            (+ any epilogue)
+  NM_RMS_WROUND = 2,// n = T(T(h*rs)*w)                      rmsnorm, add_rmsnorm
+  NM_RMS_1PW = 3,   // n = h*rs*(1+w)                        rmsnorm_gemma
+  NM_L2 = 4         // n = h*rsqrt(sum(h^2)+eps)             l2norm
+};
 
 struct NormArgs {
   const void* x;
@@ -29,231 +46,481 @@ struct NormArgs {
   int64_t ldx, ldr, ldy, ldh;
   int64_t M, N;
   float eps;
-  int norm;     // b2k_norm_kind
-  int affine;   // b2k_affine
-  int aligned;  // all row bases 16-byte aligned and N % E == 0
-  int g_target; // threads-per-row target of the register path
+  int aligned;     // all row bases 16-byte aligned and N % E == 0
+  int g_target;    // threads-per-row target of the register path
+  int tma_threads; // 0 = automatic
+  int tma_cps;     // CTAs per SM of the bulk-copy path (0 = automatic)
+  int tma_stages;  // pipeline depth (0 = automatic)
+  int use_tma;     // 0 disables the bulk-copy path
 };
 
 constexpr int kNormMaxThreads = 512;
 
-template <typename T, int ACT>
+template <typename T, int MODE, int ACT>
 int norm_launch(const NormArgs& a, cudaStream_t st);
 
 #ifdef B2K_NORM_DEFINE_KERNELS
 
-// Affine as uniform selects rather than a branch per element:
-//   n = ((h - mu) * rs) * (w + w_off) + b, optionally rounded through T twice
-//   (rmsnorm/add_rmsnorm compute T(T(h*rs) * w), specs.py:78,93).
-struct AffineSel {
-  bool has_w, has_b, rounded;
-  float w_off;
-  __device__ __forceinline__ explicit AffineSel(int affine)
-      : has_w(affine != B2K_AFF_NONE),
-        has_b(affine == B2K_AFF_WB),
-        rounded(affine == B2K_AFF_W_ROUNDED),
-        w_off(affine == B2K_AFF_ONE_PLUS_W ? 1.0f : 0.0f) {}
-};
+B2K_DEFINE_TIMEOUT_COUNTER()
 
-template <typename T, int ACT>
-__device__ __forceinline__ void norm_emit(const NormArgs& a, const AffineSel& s, T* yrow,
-                                          int64_t c, const float* hv, float mu, float rs) {
-  constexpr int E = Traits<T>::E;
+// ---------------------------------------------------------------------------
+// Affine + epilogue of one pair of elements (f32x2 arithmetic; each lane is
+// rounded exactly like the scalar reference expression).
+//   nmu2 = (-mu, -mu), rs2 = (rs, rs)
+template <typename T, int MODE, int ACT>
+__device__ __forceinline__ float2 norm_pair(float2 h, float2 nmu2, float2 rs2, float2 w,
+                                            float2 b) {
   constexpr bool P = std::is_same<T, float>::value;
-  const bool aligned = a.aligned;
-  float wv[E], bv[E], out[E];
-  if (s.has_w) {
-    load_vec<T, false>(wv, static_cast<const T*>(a.w), c, a.N, aligned);
+  float2 n;
+  if constexpr (MODE == NM_LN) {
+    n = fma2(mul2(add2(h, nmu2), rs2), w, b);
+  } else if constexpr (MODE == NM_RMS_W) {
+    n = mul2(mul2(h, rs2), w);
+  } else if constexpr (MODE == NM_RMS_WROUND) {
+    float2 t = mul2(h, rs2);
+    t = f2(round_to<T>(t.x), round_to<T>(t.y));
+    n = mul2(t, w);
+    n = f2(round_to<T>(n.x), round_to<T>(n.y));
+  } else if constexpr (MODE == NM_RMS_1PW) {
+    n = mul2(mul2(h, rs2), add2(w, f2s(1.0f)));
   } else {
-#pragma unroll
-    for (int e = 0; e < E; ++e) wv[e] = 1.0f;
+    n = mul2(h, rs2);
   }
-  if (s.has_b) {
-    load_vec<T, false>(bv, static_cast<const T*>(a.b), c, a.N, aligned);
-  } else {
-#pragma unroll
-    for (int e = 0; e < E; ++e) bv[e] = 0.0f;
-  }
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    float t = (hv[e] - mu) * rs;
-    if (s.rounded) t = round_to<T>(t);
-    float n = t * (wv[e] + s.w_off);
-    if (s.has_b) n += bv[e];
-    if (s.rounded) n = round_to<T>(n);
-    out[e] = act_apply<ACT, P>(n);
-  }
-  store_vec<T>(yrow, c, a.N, aligned, out);
+  return act_apply2<ACT, P>(n);
 }
 
-template <typename T, int V, bool RESID, int ACT>
+// ---------------------------------------------------------------------------
+// Chan et al. merge of (count, mean, M2) moments
+__device__ __forceinline__ void chan_merge(float& n, float& m, float& q, float nb, float mb,
+                                           float qb) {
+  const float nt = n + nb;
+  if (nt == 0.0f) return;
+  const float f = __fdividef(nb, nt);
+  const float d = mb - m;
+  m = fmaf(d, f, m);
+  q = q + qb + d * d * n * f;
+  n = nt;
+}
+
+// group-wide moments; `red` holds 1536 floats ([3][R<=16][32])
+__device__ __forceinline__ void group_moments(float& n, float& m, float& q, const Group& g,
+                                              float* red) {
+  const int width = g.G < 32 ? g.G : 32;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    if (o < width) {
+      const float nb = __shfl_xor_sync(0xffffffffu, n, o);
+      const float mb = __shfl_xor_sync(0xffffffffu, m, o);
+      const float qb = __shfl_xor_sync(0xffffffffu, q, o);
+      chan_merge(n, m, q, nb, mb, qb);
+    }
+  if (g.G > 32) {
+    const int nw = g.G >> 5;
+    float* rn = red;
+    float* rm = red + 512;
+    float* rq = red + 1024;
+    const int slot = g.ty * 32 + (g.tx >> 5);
+    if ((g.tx & 31) == 0) { rn[slot] = n; rm[slot] = m; rq[slot] = q; }
+    __syncthreads();
+    n = rn[g.ty * 32]; m = rm[g.ty * 32]; q = rq[g.ty * 32];
+    for (int i = 1; i < nw; ++i)
+      chan_merge(n, m, q, rn[g.ty * 32 + i], rm[g.ty * 32 + i], rq[g.ty * 32 + i]);
+    __syncthreads();
+  }
+}
+
+// Statistics of a row slice held as pairs hv[V][H] (slot v covers elements
+// [(v*G+tx)*E, +E)); out-of-range elements hold 0.  `whole` = every slot is
+// either entirely inside or entirely outside the row (aligned rows).
+template <int MODE, int V, int H>
+__device__ __forceinline__ void row_stats(const float2 (&hv)[V][H], int N, bool whole,
+                                          const Group& g, float* red, float eps, float& mu,
+                                          float& rs) {
+  constexpr int E = 2 * H;
+  if constexpr (MODE == NM_LN) {
+    float2 s2 = f2s(0.0f);
+    float cnt = 0.0f;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * g.G + g.tx) * E;
+      if (whole || c + E <= N) {
+        if (c < N) {
+#pragma unroll
+          for (int j = 0; j < H; ++j) s2 = add2(s2, hv[v][j]);
+          cnt += (float)E;
+        }
+      } else {
+        const float* hf = reinterpret_cast<const float*>(hv[v]);
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          if (c + e < N) { s2.x += hf[e]; cnt += 1.0f; }
+      }
+    }
+    float m = cnt > 0.0f ? (s2.x + s2.y) / cnt : 0.0f;
+    const float2 nm2 = f2s(-m);
+    float2 q2 = f2s(0.0f);
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * g.G + g.tx) * E;
+      if (whole || c + E <= N) {
+        if (c < N) {
+#pragma unroll
+          for (int j = 0; j < H; ++j) {
+            const float2 d = add2(hv[v][j], nm2);
+            q2 = fma2(d, d, q2);
+          }
+        }
+      } else {
+        const float* hf = reinterpret_cast<const float*>(hv[v]);
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          if (c + e < N) { const float d = hf[e] - m; q2.x = fmaf(d, d, q2.x); }
+      }
+    }
+    float q = q2.x + q2.y;
+    group_moments(cnt, m, q, g, red);
+    mu = m;
+    rs = rsqrtf(q / (float)N + eps);
+  } else {
+    float2 q2 = f2s(0.0f);
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+#pragma unroll
+      for (int j = 0; j < H; ++j) q2 = fma2(hv[v][j], hv[v][j], q2);
+    const float s = group_sum(q2.x + q2.y, g, red);
+    mu = 0.0f;
+    rs = rsqrtf((MODE == NM_L2 ? s : s / (float)N) + eps);
+  }
+}
+
+// pairs of one 16-byte slot from global memory (aligned: one vector load;
+// otherwise bounds-checked scalars); out-of-range elements read as 0
+template <typename T, bool STREAM>
+__device__ __forceinline__ void load_pairs(float2* f, const T* row, int c, int N, bool aligned) {
+  load_vec<T, STREAM>(reinterpret_cast<float*>(f), row, c, N, aligned);
+}
+template <typename T>
+__device__ __forceinline__ void store_pairs(T* row, int c, int N, bool aligned, const float2* f) {
+  store_vec<T>(row, c, N, aligned, reinterpret_cast<const float*>(f));
+}
+
+// ---------------------------------------------------------------------------
+// register path
+template <typename T, int V, bool RESID, int MODE, int ACT>
 __global__ void __launch_bounds__(kNormMaxThreads) norm_rows_kernel(const NormArgs a) {
   constexpr int E = Traits<T>::E;
-  __shared__ float red[1024];
+  constexpr int H = E / 2;
+  constexpr bool HAS_W = MODE != NM_L2;
+  __shared__ float red[1536];
   const Group g;
   const int64_t row = (int64_t)blockIdx.x * blockDim.y + g.ty;
   const bool valid = row < a.M;
-  const int64_t N = a.N;
+  const int N = (int)a.N;
   const bool aligned = a.aligned;
   const T* xr = static_cast<const T*>(a.x) + (valid ? row * a.ldx : 0);
   const T* rr = RESID ? static_cast<const T*>(a.r) + (valid ? row * a.ldr : 0) : nullptr;
 
-  // ---- one read of the row (x and r), h = x + r in fp32 -------------------
-  float hv[V][E];
+  float2 hv[V][H];
 #pragma unroll
   for (int v = 0; v < V; ++v) {
-    const int64_t c = (int64_t)(v * g.G + g.tx) * E;
+    const int c = (v * g.G + g.tx) * E;
     if (valid) {
-      load_vec<T, true>(hv[v], xr, c, N, aligned);
+      load_pairs<T, true>(hv[v], xr, c, N, aligned);
     } else {
 #pragma unroll
-      for (int e = 0; e < E; ++e) hv[v][e] = 0.0f;
+      for (int j = 0; j < H; ++j) hv[v][j] = f2s(0.0f);
     }
   }
   if (RESID && valid) {
 #pragma unroll
     for (int v = 0; v < V; ++v) {
-      float t[E];
-      load_vec<T, true>(t, rr, (int64_t)(v * g.G + g.tx) * E, N, aligned);
+      float2 t[H];
+      load_pairs<T, true>(t, rr, (v * g.G + g.tx) * E, N, aligned);
 #pragma unroll
-      for (int e = 0; e < E; ++e) hv[v][e] += t[e];
+      for (int j = 0; j < H; ++j) hv[v][j] = add2(hv[v][j], t[j]);
     }
   }
-  // residual stream output T(x + r), issued before the reductions
   if (a.h != nullptr && valid) {
     T* hrow = static_cast<T*>(a.h) + row * a.ldh;
 #pragma unroll
-    for (int v = 0; v < V; ++v) store_vec<T>(hrow, (int64_t)(v * g.G + g.tx) * E, N, aligned, hv[v]);
+    for (int v = 0; v < V; ++v) store_pairs<T>(hrow, (v * g.G + g.tx) * E, N, aligned, hv[v]);
   }
 
-  // ---- statistics --------------------------------------------------------
-  float mu = 0.0f, rs;
-  if (a.norm == B2K_NORM_LN) {
-    float s = 0.0f;
-#pragma unroll
-    for (int v = 0; v < V; ++v)
-#pragma unroll
-      for (int e = 0; e < E; ++e) s += hv[v][e];
-    s = group_sum(s, g, red);
-    mu = s / (float)N;
-    float q = 0.0f;
-#pragma unroll
-    for (int v = 0; v < V; ++v) {
-      const int64_t c = (int64_t)(v * g.G + g.tx) * E;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const float d = (c + e < N) ? hv[v][e] - mu : 0.0f;
-        q += d * d;
-      }
-    }
-    q = group_sum(q, g, red);
-    rs = rsqrtf(q / (float)N + a.eps);
-  } else {
-    float s = 0.0f;
-#pragma unroll
-    for (int v = 0; v < V; ++v)
-#pragma unroll
-      for (int e = 0; e < E; ++e) s += hv[v][e] * hv[v][e];
-    s = group_sum(s, g, red);
-    rs = rsqrtf((a.norm == B2K_NORM_L2 ? s : s / (float)N) + a.eps);
-  }
+  float mu, rs;
+  row_stats<MODE, V, H>(hv, N, aligned, g, red, a.eps, mu, rs);
   if (!valid) return;
 
-  // ---- affine + epilogue + one write ---------------------------------------
-  const AffineSel sel(a.affine);
+  const float2 nmu2 = f2s(-mu), rs2 = f2s(rs);
   T* yrow = static_cast<T*>(a.y) + row * a.ldy;
 #pragma unroll
-  for (int v = 0; v < V; ++v)
-    norm_emit<T, ACT>(a, sel, yrow, (int64_t)(v * g.G + g.tx) * E, hv[v], mu, rs);
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * g.G + g.tx) * E;
+    float2 wv[H], bv[H], out[H];
+    if constexpr (HAS_W) load_pairs<T, false>(wv, static_cast<const T*>(a.w), c, N, aligned);
+    if constexpr (MODE == NM_LN) load_pairs<T, false>(bv, static_cast<const T*>(a.b), c, N, aligned);
+#pragma unroll
+    for (int j = 0; j < H; ++j)
+      out[j] = norm_pair<T, MODE, ACT>(hv[v][j], nmu2, rs2, HAS_W ? wv[j] : f2s(1.0f),
+                                       MODE == NM_LN ? bv[j] : f2s(0.0f));
+    store_pairs<T>(yrow, c, N, aligned, out);
+  }
 }
 
-// Rows too long for registers: one row per block; the statistics pass(es)
-// read with the default L2 policy so the final pass re-reads the row from L2.
-template <typename T, bool RESID, int ACT>
+// rows longer than the register budget: one row per block, statistics from
+// L2-friendly re-reads (LayerNorm: mean pass, centred-variance pass)
+template <typename T, bool RESID, int MODE, int ACT>
 __global__ void __launch_bounds__(kNormMaxThreads) norm_rows_stream_kernel(const NormArgs a) {
   constexpr int E = Traits<T>::E;
-  __shared__ float red[1024];
+  constexpr int H = E / 2;
+  constexpr bool HAS_W = MODE != NM_L2;
+  __shared__ float red[1536];
   const Group g;
   const int64_t row = blockIdx.x;
-  const int64_t N = a.N;
+  const int N = (int)a.N;
   const bool aligned = a.aligned;
   const T* xr = static_cast<const T*>(a.x) + row * a.ldx;
   const T* rr = RESID ? static_cast<const T*>(a.r) + row * a.ldr : nullptr;
   T* hrow = a.h ? static_cast<T*>(a.h) + row * a.ldh : nullptr;
-  const int64_t step = (int64_t)g.G * E;
-  const bool ln = a.norm == B2K_NORM_LN;
+  const int step = g.G * E;
 
-  auto load_h = [&](float* hv, int64_t c) {
-    load_vec<T, false>(hv, xr, c, N, aligned);
+  auto load_h = [&](float2* hv, int c) {
+    load_pairs<T, false>(hv, xr, c, N, aligned);
     if (RESID) {
-      float t[E];
-      load_vec<T, false>(t, rr, c, N, aligned);
+      float2 t[H];
+      load_pairs<T, false>(t, rr, c, N, aligned);
 #pragma unroll
-      for (int e = 0; e < E; ++e) hv[e] += t[e];
+      for (int j = 0; j < H; ++j) hv[j] = add2(hv[j], t[j]);
     }
   };
 
   float mu = 0.0f, rs;
-  float s = 0.0f;
-  for (int64_t c = (int64_t)g.tx * E; c < N; c += step) {
-    float hv[E];
+  float2 s2 = f2s(0.0f);
+  for (int c = g.tx * E; c < N; c += step) {
+    float2 hv[H];
     load_h(hv, c);
-    if (hrow) store_vec<T>(hrow, c, N, aligned, hv);
+    if (hrow) store_pairs<T>(hrow, c, N, aligned, hv);
 #pragma unroll
-    for (int e = 0; e < E; ++e) s += ln ? hv[e] : hv[e] * hv[e];
+    for (int j = 0; j < H; ++j) s2 = (MODE == NM_LN) ? add2(s2, hv[j]) : fma2(hv[j], hv[j], s2);
   }
-  s = group_sum(s, g, red);
-  if (ln) {
+  const float s = group_sum(s2.x + s2.y, g, red);
+  if constexpr (MODE == NM_LN) {
     mu = s / (float)N;
     float q = 0.0f;
-    for (int64_t c = (int64_t)g.tx * E; c < N; c += step) {
-      float hv[E];
+    for (int c = g.tx * E; c < N; c += step) {
+      float2 hv[H];
       load_h(hv, c);
+      const float* hf = reinterpret_cast<const float*>(hv);
 #pragma unroll
       for (int e = 0; e < E; ++e) {
-        const float d = (c + e < N) ? hv[e] - mu : 0.0f;
-        q += d * d;
+        const float d = (c + e < N) ? hf[e] - mu : 0.0f;
+        q = fmaf(d, d, q);
       }
     }
     q = group_sum(q, g, red);
     rs = rsqrtf(q / (float)N + a.eps);
   } else {
-    rs = rsqrtf((a.norm == B2K_NORM_L2 ? s : s / (float)N) + a.eps);
+    rs = rsqrtf((MODE == NM_L2 ? s : s / (float)N) + a.eps);
   }
-  const AffineSel sel(a.affine);
+  const float2 nmu2 = f2s(-mu), rs2 = f2s(rs);
   T* yrow = static_cast<T*>(a.y) + row * a.ldy;
-  for (int64_t c = (int64_t)g.tx * E; c < N; c += step) {
-    float hv[E];
+  for (int c = g.tx * E; c < N; c += step) {
+    float2 hv[H], wv[H], bv[H], out[H];
     load_h(hv, c);
-    norm_emit<T, ACT>(a, sel, yrow, c, hv, mu, rs);
+    if constexpr (HAS_W) load_pairs<T, false>(wv, static_cast<const T*>(a.w), c, N, aligned);
+    if constexpr (MODE == NM_LN) load_pairs<T, false>(bv, static_cast<const T*>(a.b), c, N, aligned);
+#pragma unroll
+    for (int j = 0; j < H; ++j)
+      out[j] = norm_pair<T, MODE, ACT>(hv[j], nmu2, rs2, HAS_W ? wv[j] : f2s(1.0f),
+                                       MODE == NM_LN ? bv[j] : f2s(0.0f));
+    store_pairs<T>(yrow, c, N, aligned, out);
   }
 }
 
-template <typename T, bool RESID, int ACT>
+// ---------------------------------------------------------------------------
+// bulk-copy pipelined path (aligned rows only)
+template <typename T, int V, bool RESID, int MODE, int ACT>
+__global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArgs a, const int S) {
+  constexpr int E = Traits<T>::E;
+  constexpr int H = E / 2;
+  constexpr bool HAS_W = MODE != NM_L2;
+  extern __shared__ __align__(128) unsigned char dsm[];
+  __shared__ float red[1536];
+  __shared__ volatile int abort_flag;
+  const Group g;  // G = blockDim.x, one row at a time
+  const int N = (int)a.N;
+  const uint32_t row_bytes = (uint32_t)N * (uint32_t)sizeof(T);
+  const uint32_t stage_bytes = (RESID ? 2u : 1u) * row_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + (size_t)S * stage_bytes);
+  const int64_t first = blockIdx.x, stride = gridDim.x;
+  const int64_t nrows = first < a.M ? (a.M - 1 - first) / stride + 1 : 0;
+  const T* xg = static_cast<const T*>(a.x);
+  const T* rg = static_cast<const T*>(a.r);
+
+  auto issue = [&](int64_t k) {
+    const int s = (int)(k % S);
+    const int64_t row = first + k * stride;
+    unsigned char* st = dsm + (size_t)s * stage_bytes;
+    mbar_arrive_expect_tx(&full[s], stage_bytes);
+    bulk_g2s(st, xg + row * a.ldx, row_bytes, &full[s]);
+    if (RESID) bulk_g2s(st + row_bytes, rg + row * a.ldr, row_bytes, &full[s]);
+  };
+
+  if (g.tx == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+    fence_barrier_init();
+    abort_flag = 0;
+  }
+  __syncthreads();
+  int64_t issued = 0;
+  if (g.tx == 0)
+    for (; issued < nrows && issued < S; ++issued) issue(issued);
+
+  // weight slices stay in registers (raw 16-byte vectors) for every row
+  uint4 wraw[V], braw[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * g.G + g.tx) * E;
+    wraw[v] = (HAS_W && c < N) ? ld_keep(static_cast<const T*>(a.w) + c) : zero4();
+    braw[v] = (MODE == NM_LN && c < N) ? ld_keep(static_cast<const T*>(a.b) + c) : zero4();
+  }
+
+  int64_t k = 0;
+  for (; k < nrows; ++k) {
+    const int s = (int)(k % S);
+    const uint32_t parity = (uint32_t)((k / S) & 1);
+    if (!mbar_wait(&full[s], parity)) {
+      abort_flag = 1;  // garbage row; every thread leaves after the reduction
+      atomicAdd(&b2k_tu_timeouts, 1u);
+    }
+    const T* xs = reinterpret_cast<const T*>(dsm + (size_t)s * stage_bytes);
+    const T* rsm = xs + N;
+    const int64_t row = first + k * stride;
+    float2 hv[V][H];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * g.G + g.tx) * E;
+      if (c < N) {
+        unpack2<T>(*reinterpret_cast<const uint4*>(xs + c), hv[v]);
+        if (RESID) {
+          float2 t[H];
+          unpack2<T>(*reinterpret_cast<const uint4*>(rsm + c), t);
+#pragma unroll
+          for (int j = 0; j < H; ++j) hv[v][j] = add2(hv[v][j], t[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < H; ++j) hv[v][j] = f2s(0.0f);
+      }
+    }
+    if (a.h != nullptr) {
+      T* hrow = static_cast<T*>(a.h) + row * a.ldh;
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const int c = (v * g.G + g.tx) * E;
+        if (c < N) st_stream(hrow + c, pack2<T>(hv[v]));
+      }
+    }
+    float mu, rs;
+    row_stats<MODE, V, H>(hv, N, true, g, red, a.eps, mu, rs);
+    // the reduction's barriers order every thread's reads of stage s before
+    // the refill below
+    if (abort_flag) break;
+    if (g.tx == 0 && issued < nrows) {
+      fence_proxy_async();
+      issue(issued);
+      ++issued;
+    }
+    const float2 nmu2 = f2s(-mu), rs2 = f2s(rs);
+    T* yrow = static_cast<T*>(a.y) + row * a.ldy;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * g.G + g.tx) * E;
+      if (c < N) {
+        float2 wv[H], bv[H], out[H];
+        if constexpr (HAS_W) unpack2<T>(wraw[v], wv);
+        if constexpr (MODE == NM_LN) unpack2<T>(braw[v], bv);
+#pragma unroll
+        for (int j = 0; j < H; ++j)
+          out[j] = norm_pair<T, MODE, ACT>(hv[v][j], nmu2, rs2, HAS_W ? wv[j] : f2s(1.0f),
+                                           MODE == NM_LN ? bv[j] : f2s(0.0f));
+        st_stream(yrow + c, pack2<T>(out));
+      }
+    }
+  }
+  // after an abort, wait (bounded) for the copies still in flight so none
+  // lands in shared memory after the block has exited
+  if (g.tx == 0)
+    for (int64_t j = k; j < issued; ++j)
+      mbar_wait(&full[(int)(j % S)], (uint32_t)((j / S) & 1));
+}
+
+// ---------------------------------------------------------------------------
+// launch
+template <typename T, bool RESID, int MODE, int ACT>
+static bool norm_try_tma(const NormArgs& a, cudaStream_t st, int* status) {
+  constexpr int E = Traits<T>::E;
+  if (!a.use_tma || !a.aligned) return false;
+  const int64_t nvec = a.N / E;
+  if (nvec < 256) return false;  // short rows: register path packs several rows per block
+  const int64_t stage = (RESID ? 2 : 1) * a.N * (int64_t)sizeof(T);
+  if (stage > (64 << 10)) return false;
+  int G = a.tma_threads;
+  if (G <= 0) {
+    G = next_pow2((nvec + 3) / 4);
+    G = G < 64 ? 64 : (G > kNormMaxThreads ? kNormMaxThreads : G);
+  }
+  const int64_t vneed = (nvec + G - 1) / G;
+  if (vneed > 8) return false;
+  const int V = vneed <= 4 ? 4 : 8;
+  const int sms = sm_count();
+  int cps = a.tma_cps > 0 ? a.tma_cps : 2;
+  const int64_t budget = 200 << 10;  // dynamic shared memory per SM (static use ~6 KB/CTA)
+  int S = a.tma_stages > 0 ? a.tma_stages : 4;
+  while (S > 2 && (int64_t)cps * S * stage > budget) --S;
+  while (cps > 1 && (int64_t)cps * S * stage > budget) --cps;
+  if ((int64_t)cps * S * stage > budget) return false;
+  const size_t smem = (size_t)S * stage + (size_t)S * sizeof(uint64_t);
+  int64_t grid = (int64_t)sms * cps;
+  if (grid > a.M) grid = a.M;
+
+  auto go = [&](auto kern) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<(unsigned)grid, G, smem, st>>>(a, S);
+  };
+  if (V == 4) go(norm_tma_kernel<T, 4, RESID, MODE, ACT>);
+  else go(norm_tma_kernel<T, 8, RESID, MODE, ACT>);
+  *status = check_launch("b2k_norm(tma)");
+  return true;
+}
+
+template <typename T, bool RESID, int MODE, int ACT>
 static int norm_launch_resid(const NormArgs& a, cudaStream_t st) {
   constexpr int E = Traits<T>::E;
+  int status;
+  if (norm_try_tma<T, RESID, MODE, ACT>(a, st, &status)) return status;
   RowCfg cfg;
-  if (choose_row_cfg(a.N, E, a.g_target, &cfg, 8, kNormMaxThreads)) {
+  if (choose_row_cfg(a.N, E, a.g_target, &cfg, 4, kNormMaxThreads)) {
     const dim3 block(cfg.G, cfg.R);
     const int64_t grid = (a.M + cfg.R - 1) / cfg.R;
     switch (cfg.V) {
-      case 1: norm_rows_kernel<T, 1, RESID, ACT><<<grid, block, 0, st>>>(a); break;
-      case 2: norm_rows_kernel<T, 2, RESID, ACT><<<grid, block, 0, st>>>(a); break;
-      case 4: norm_rows_kernel<T, 4, RESID, ACT><<<grid, block, 0, st>>>(a); break;
-      default: norm_rows_kernel<T, 8, RESID, ACT><<<grid, block, 0, st>>>(a); break;
+      case 1: norm_rows_kernel<T, 1, RESID, MODE, ACT><<<grid, block, 0, st>>>(a); break;
+      case 2: norm_rows_kernel<T, 2, RESID, MODE, ACT><<<grid, block, 0, st>>>(a); break;
+      default: norm_rows_kernel<T, 4, RESID, MODE, ACT><<<grid, block, 0, st>>>(a); break;
     }
   } else {
-    norm_rows_stream_kernel<T, RESID, ACT><<<a.M, dim3(kNormMaxThreads, 1), 0, st>>>(a);
+    norm_rows_stream_kernel<T, RESID, MODE, ACT><<<a.M, dim3(kNormMaxThreads, 1), 0, st>>>(a);
   }
   return check_launch("b2k_norm");
 }
 
-template <typename T, int ACT>
+template <typename T, int MODE, int ACT>
 int norm_launch(const NormArgs& a, cudaStream_t st) {
-  return a.r ? norm_launch_resid<T, true, ACT>(a, st) : norm_launch_resid<T, false, ACT>(a, st);
+  return a.r ? norm_launch_resid<T, true, MODE, ACT>(a, st)
+             : norm_launch_resid<T, false, MODE, ACT>(a, st);
 }
 
-#define B2K_NORM_INSTANTIATE(T, ACT) template int norm_launch<T, ACT>(const NormArgs&, cudaStream_t);
+#define B2K_NORM_INSTANTIATE(T, MODE, ACT) \
+  template int norm_launch<T, MODE, ACT>(const NormArgs&, cudaStream_t);
 
 #endif  // B2K_NORM_DEFINE_KERNELS
 

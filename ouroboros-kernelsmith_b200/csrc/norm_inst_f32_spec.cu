@@ -1,0 +1,9 @@
+// Instances of the norm-family kernels for float: spec.
+#define B2K_NORM_DEFINE_KERNELS
+#include "norm_impl.cuh"
+
+namespace b2k {
+B2K_NORM_INSTANTIATE(float, NM_RMS_WROUND, 0)
+B2K_NORM_INSTANTIATE(float, NM_RMS_1PW, 0)
+B2K_NORM_INSTANTIATE(float, NM_L2, 0)
+}  // namespace b2k

@@ -1,0 +1,103 @@
+// Bulk-copy (TMA) and mbarrier primitives for the row pipelines (sm_90+ PTX,
+// used here on sm_100a).  Only the untiled global->shared bulk copy is used,
+// always from this GPU's own memory and never with .multicast::cluster.
+//
+// Every wait is bounded: after kTimeoutNs of global time without progress the
+// wait gives up, the kernel bumps its translation unit's timeout counter
+// (read on the host with b2k_pipeline_timeouts) and leaves the loop.
+#pragma once
+
+#include "common.cuh"
+
+namespace b2k {
+
+constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+// Makes barrier initialisation (generic proxy) visible to the async proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Orders this thread's earlier shared-memory accesses before its later
+// async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// global -> shared bulk copy of `bytes` (multiple of 16, both addresses
+// 16-byte aligned) completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait for the phase with `parity` to complete.  Returns false on
+// timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer() - t0 > kTimeoutNs) return false;
+  }
+}
+
+// Host-side registry of per-translation-unit timeout counters.
+using TimeoutReader = unsigned (*)(bool reset);
+void register_timeout_reader(TimeoutReader f);
+
+}  // namespace b2k
+
+// Defines this translation unit's device timeout counter `b2k_tu_timeouts`
+// and registers its host reader.  Use once per .cu file that launches a
+// pipelined kernel (before the kernels).
+#define B2K_DEFINE_TIMEOUT_COUNTER()                                                     \
+  static __device__ unsigned b2k_tu_timeouts;                                          \
+  static unsigned b2k_read_tu_timeouts(bool reset) {                                     \
+    unsigned v = 0;                                                                      \
+    if (cudaMemcpyFromSymbol(&v, b2k_tu_timeouts, sizeof(v)) != cudaSuccess) return 0;   \
+    if (reset && v) {                                                                    \
+      const unsigned z = 0;                                                              \
+      cudaMemcpyToSymbol(b2k_tu_timeouts, &z, sizeof(z));                                \
+    }                                                                                    \
+    return v;                                                                            \
+  }                                                                                      \
+  static const int b2k_tu_timeouts_registered =                                          \
+      (::b2k::register_timeout_reader(&b2k_read_tu_timeouts), 0);

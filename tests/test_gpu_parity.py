@@ -65,3 +65,9 @@ def test_bench_shape_sampled_rows(op):
     ref = regimes.reference(op, sub)
     ok, err, bad = run_checked(op, run, case, ref, rows=rows)
     assert ok, f"{op} bench shape: max err {err} ({bad} bad)"
+
+
+def test_zz_no_pipeline_timeouts():
+    """No bounded pipeline wait gave up during the parity runs above."""
+    torch.cuda.synchronize()
+    assert _lib.lib.b2k_pipeline_timeouts(1) == 0
