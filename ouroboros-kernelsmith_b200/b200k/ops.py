@@ -514,3 +514,32 @@ def kl_div(x, y):
         st = L.lib.b2k_kl_div(_p(x2), ldx, _p(y2), ldy, _p(out), m, n, dt, stream)
     L.check(st, "b2k_kl_div")
     return out.view(x.shape[:-1])
+
+
+def cross_entropy_mean(logits, tgt, ignore_index: int = -100, group=None):
+    """Mean cross-entropy over the rows whose target is not ignore_index, as a
+    0-dim fp32 tensor on the logits' device.  With a process group, `logits`
+    and `tgt` are this rank's row shard and the mean is over all ranks' rows
+    (one NCCL all-reduce of [loss sum, valid count]).  Per-row losses are the
+    spec op's (specs.py:239-241) in fp32; their sum is accumulated in fp64 in
+    a fixed order."""
+    from .dist import allreduce_sumcount
+    dev = _cuda(logits, tgt)
+    dt = _dtype_id(logits)
+    n = logits.shape[-1]
+    x2, ldx = _rows(logits, n)
+    m = x2.shape[0]
+    t1 = _check_tgt(tgt, m, dev)
+    row_loss = torch.empty((m,), dtype=torch.float32, device=dev)
+    sumcount = torch.empty((2,), dtype=torch.float64, device=dev)
+    out = torch.empty((), dtype=torch.float32, device=dev)
+    with _dev(dev) as stream:
+        st = L.lib.b2k_cross_entropy(_p(x2), ldx, _p(t1), _p(row_loss), m, n, dt, L.F32,
+                                     ignore_index, stream)
+        L.check(st, "b2k_cross_entropy")
+        L.check(L.lib.b2k_ce_reduce(_p(row_loss), _p(t1), m, ignore_index, _p(sumcount), stream),
+                "b2k_ce_reduce")
+    allreduce_sumcount(sumcount, group)
+    with _dev(dev) as stream:
+        L.check(L.lib.b2k_ce_mean(_p(sumcount), _p(out), stream), "b2k_ce_mean")
+    return out

@@ -23,7 +23,7 @@
 #pragma once
 
 #include "rowio.cuh"
-#include "tma.cuh"
+#include "rowpipe.cuh"
 
 namespace b2k {
 
@@ -343,37 +343,17 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
   constexpr int E = Traits<T>::E;
   constexpr int H = E / 2;
   constexpr bool HAS_W = MODE != NM_L2;
+  constexpr int NIN = RESID ? 2 : 1;
   extern __shared__ __align__(128) unsigned char dsm[];
   __shared__ float red[1536];
   __shared__ volatile int abort_flag;
   const Group g;  // G = blockDim.x, one row at a time
   const int N = (int)a.N;
-  const uint32_t row_bytes = (uint32_t)N * (uint32_t)sizeof(T);
-  const uint32_t stage_bytes = (RESID ? 2u : 1u) * row_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + (size_t)S * stage_bytes);
-  const int64_t first = blockIdx.x, stride = gridDim.x;
-  const int64_t nrows = first < a.M ? (a.M - 1 - first) / stride + 1 : 0;
-  const T* xg = static_cast<const T*>(a.x);
-  const T* rg = static_cast<const T*>(a.r);
-
-  auto issue = [&](int64_t k) {
-    const int s = (int)(k % S);
-    const int64_t row = first + k * stride;
-    unsigned char* st = dsm + (size_t)s * stage_bytes;
-    mbar_arrive_expect_tx(&full[s], stage_bytes);
-    bulk_g2s(st, xg + row * a.ldx, row_bytes, &full[s]);
-    if (RESID) bulk_g2s(st + row_bytes, rg + row * a.ldr, row_bytes, &full[s]);
-  };
-
-  if (g.tx == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
-    fence_barrier_init();
-    abort_flag = 0;
-  }
-  __syncthreads();
-  int64_t issued = 0;
-  if (g.tx == 0)
-    for (; issued < nrows && issued < S; ++issued) issue(issued);
+  if (g.tx == 0) abort_flag = 0;
+  RowPipe<NIN> pipe;
+  const void* srcs[2] = {a.x, a.r};
+  const int64_t lds[2] = {a.ldx, a.ldr};
+  pipe.init(dsm, S, a.M, (uint32_t)N * (uint32_t)sizeof(T), srcs, lds, (int)sizeof(T));
 
   // weight slices stay in registers (raw 16-byte vectors) for every row
   uint4 wraw[V], braw[V];
@@ -385,16 +365,15 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
   }
 
   int64_t k = 0;
-  for (; k < nrows; ++k) {
-    const int s = (int)(k % S);
-    const uint32_t parity = (uint32_t)((k / S) & 1);
-    if (!mbar_wait(&full[s], parity)) {
+  for (; k < pipe.nrows; ++k) {
+    bool ok;
+    const T* xs = reinterpret_cast<const T*>(pipe.wait_next(ok));
+    if (!ok) {
       abort_flag = 1;  // garbage row; every thread leaves after the reduction
       atomicAdd(&b2k_tu_timeouts, 1u);
     }
-    const T* xs = reinterpret_cast<const T*>(dsm + (size_t)s * stage_bytes);
     const T* rsm = xs + N;
-    const int64_t row = first + k * stride;
+    const int64_t row = pipe.row_of(k);
     float2 hv[V][H];
 #pragma unroll
     for (int v = 0; v < V; ++v) {
@@ -422,14 +401,10 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
     }
     float mu, rs;
     row_stats<MODE, V, H>(hv, N, true, g, red, a.eps, mu, rs);
-    // the reduction's barriers order every thread's reads of stage s before
-    // the refill below
+    // the reduction's barriers order every thread's reads of the stage
+    // before the refill
     if (abort_flag) break;
-    if (g.tx == 0 && issued < nrows) {
-      fence_proxy_async();
-      issue(issued);
-      ++issued;
-    }
+    pipe.refill();
     const float2 nmu2 = f2s(-mu), rs2 = f2s(rs);
     T* yrow = static_cast<T*>(a.y) + row * a.ldy;
 #pragma unroll
@@ -447,11 +422,7 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
       }
     }
   }
-  // after an abort, wait (bounded) for the copies still in flight so none
-  // lands in shared memory after the block has exited
-  if (g.tx == 0)
-    for (int64_t j = k; j < issued; ++j)
-      mbar_wait(&full[(int)(j % S)], (uint32_t)((j / S) & 1));
+  pipe.drain(k);
 }
 
 // ---------------------------------------------------------------------------
@@ -473,13 +444,10 @@ static bool norm_try_tma(const NormArgs& a, cudaStream_t st, int* status) {
   if (vneed > 8) return false;
   const int V = vneed <= 4 ? 4 : 8;
   const int sms = sm_count();
-  int cps = a.tma_cps > 0 ? a.tma_cps : 2;
-  const int64_t budget = 200 << 10;  // dynamic shared memory per SM (static use ~6 KB/CTA)
-  int S = a.tma_stages > 0 ? a.tma_stages : 4;
-  while (S > 2 && (int64_t)cps * S * stage > budget) --S;
-  while (cps > 1 && (int64_t)cps * S * stage > budget) --cps;
-  if ((int64_t)cps * S * stage > budget) return false;
-  const size_t smem = (size_t)S * stage + (size_t)S * sizeof(uint64_t);
+  PipeShape ps;
+  if (!choose_pipe_shape(stage, a.tma_cps, a.tma_stages, &ps)) return false;
+  const int cps = ps.cps, S = ps.S;
+  const size_t smem = RowPipe<RESID ? 2 : 1>::smem_bytes(S, a.N * (int64_t)sizeof(T));
   int64_t grid = (int64_t)sms * cps;
   if (grid > a.M) grid = a.M;
 

@@ -1,0 +1,447 @@
+// Rotary embeddings (ouroboros/specs.py:96-102 rotate_half, :228-236
+// interleaved pairs, :133-143 and :193-198 RMSNorm + RoPE).
+//
+// b2k_rope (spec layout, per-row tables): one work item = one 16-byte vector
+// of x together with its partner (the vector D/2 away for the half-split
+// form, or the E/2 table entries of its pairs for the interleaved form).
+// b2k_rope_qk (attention layout): one block per (batch, position); its
+// threads cover every head of q and k for that position, so the position's
+// table row is read from HBM once and served from L1 for all heads; q and k
+// are rotated in the same launch.
+// b2k_norm_rope: RMSNorm over the head dim in registers, the normalised row
+// staged in shared memory so each element can read its rotation partner.
+#include "rowio.cuh"
+
+namespace b2k {
+
+constexpr int kRopeThreads = 256;
+
+// ---------------------------------------------------------------- spec layout
+struct RopeArgs {
+  const void* x;
+  const void* cos;
+  const void* sin;
+  void* y;
+  int64_t ldx, ldc, lds, ldy, M;
+  int D;
+};
+
+// half-split, vector path: item = (row, j), j-th vector of the first half
+template <typename T>
+__global__ void __launch_bounds__(kRopeThreads) rope_half_vec_kernel(const RopeArgs a,
+                                                                     int64_t items, int vph) {
+  constexpr int E = Traits<T>::E;
+  const int h = a.D / 2;
+  for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = it / vph;
+    const int c = (int)(it - row * vph) * E;
+    const T* xr = static_cast<const T*>(a.x) + row * a.ldx;
+    const T* cr = static_cast<const T*>(a.cos) + row * a.ldc;
+    const T* sr = static_cast<const T*>(a.sin) + row * a.lds;
+    float x1[E], x2[E], c1[E], c2[E], s1[E], s2[E], o1[E], o2[E];
+    unpack<T>(ld_stream(xr + c), x1);
+    unpack<T>(ld_stream(xr + c + h), x2);
+    unpack<T>(ld_stream(cr + c), c1);
+    unpack<T>(ld_stream(cr + c + h), c2);
+    unpack<T>(ld_stream(sr + c), s1);
+    unpack<T>(ld_stream(sr + c + h), s2);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      o1[e] = x1[e] * c1[e] - x2[e] * s1[e];
+      o2[e] = x2[e] * c2[e] + x1[e] * s2[e];
+    }
+    T* yr = static_cast<T*>(a.y) + row * a.ldy;
+    st_stream(yr + c, pack<T>(o1));
+    st_stream(yr + c + h, pack<T>(o2));
+  }
+}
+
+// interleaved, vector path: item = (row, j), j-th vector of x (E/2 pairs)
+template <typename T>
+__global__ void __launch_bounds__(kRopeThreads) rope_inter_vec_kernel(const RopeArgs a,
+                                                                      int64_t items, int vpr) {
+  constexpr int E = Traits<T>::E;
+  constexpr int H = E / 2;
+  for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = it / vpr;
+    const int c = (int)(it - row * vpr) * E;
+    const T* xr = static_cast<const T*>(a.x) + row * a.ldx;
+    const T* cr = static_cast<const T*>(a.cos) + row * a.ldc + c / 2;
+    const T* sr = static_cast<const T*>(a.sin) + row * a.lds + c / 2;
+    float xv[E], cv[H], sv[H], o[E];
+    unpack<T>(ld_stream(xr + c), xv);
+    // E/2 table entries = 8 bytes
+    const uint2 cw = __ldcs(reinterpret_cast<const uint2*>(cr));
+    const uint2 sw = __ldcs(reinterpret_cast<const uint2*>(sr));
+    {
+      float tmp[2 * H];
+      unpack<T>(make_uint4(cw.x, cw.y, sw.x, sw.y), tmp);
+#pragma unroll
+      for (int i = 0; i < H; ++i) { cv[i] = tmp[i]; sv[i] = tmp[H + i]; }
+    }
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+      o[2 * i] = xv[2 * i] * cv[i] - xv[2 * i + 1] * sv[i];
+      o[2 * i + 1] = xv[2 * i + 1] * cv[i] + xv[2 * i] * sv[i];
+    }
+    st_stream(static_cast<T*>(a.y) + row * a.ldy + c, pack<T>(o));
+  }
+}
+
+// any shape: item = (row, i) for i < D/2, one rotation pair per item
+template <typename T, bool INTER>
+__global__ void __launch_bounds__(kRopeThreads) rope_scalar_kernel(const RopeArgs a) {
+  const int h = a.D / 2;
+  const int64_t items = a.M * h;
+  for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = it / h;
+    const int i = (int)(it - row * h);
+    const T* xr = static_cast<const T*>(a.x) + row * a.ldx;
+    const T* cr = static_cast<const T*>(a.cos) + row * a.ldc;
+    const T* sr = static_cast<const T*>(a.sin) + row * a.lds;
+    T* yr = static_cast<T*>(a.y) + row * a.ldy;
+    if (INTER) {
+      const float x1 = ld1(xr + 2 * i), x2 = ld1(xr + 2 * i + 1);
+      const float c = ld1(cr + i), s = ld1(sr + i);
+      st1(yr + 2 * i, x1 * c - x2 * s);
+      st1(yr + 2 * i + 1, x2 * c + x1 * s);
+    } else {
+      const float x1 = ld1(xr + i), x2 = ld1(xr + i + h);
+      st1(yr + i, x1 * ld1(cr + i) - x2 * ld1(sr + i));
+      st1(yr + i + h, x2 * ld1(cr + i + h) + x1 * ld1(sr + i + h));
+    }
+  }
+}
+
+// ---------------------------------------------------------------- attention layout
+struct RopeQkArgs {
+  const void* q;
+  const void* k;
+  const void* cos;
+  const void* sin;
+  void* qo;
+  void* ko;
+  int64_t B, S, H, Hk;
+  int D;
+};
+
+template <typename T, bool INTER>
+__global__ void __launch_bounds__(1024) rope_qk_kernel(const RopeQkArgs a, int per_head) {
+  constexpr int E = Traits<T>::E;
+  constexpr int HP = E / 2;
+  const int64_t p = blockIdx.x;  // b * S + s
+  const int64_t s = p % a.S;
+  const int D = a.D, half = D / 2;
+  const int heads = (int)(a.H + a.Hk);
+  const T* ct = static_cast<const T*>(a.cos) + s * half;
+  const T* st = static_cast<const T*>(a.sin) + s * half;
+  const int items = heads * per_head;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int hh = it / per_head;
+    const int j = it - hh * per_head;
+    const bool isq = hh < a.H;
+    const int64_t base = isq ? (p * a.H + hh) * D : (p * a.Hk + (hh - a.H)) * D;
+    const T* src = (isq ? static_cast<const T*>(a.q) : static_cast<const T*>(a.k)) + base;
+    T* dst = (isq ? static_cast<T*>(a.qo) : static_cast<T*>(a.ko)) + base;
+    if (!INTER) {
+      const int c = j * E;  // first-half offset; partner at c + half
+      float x1[E], x2[E], cv[E], sv[E], o1[E], o2[E];
+      unpack<T>(ld_stream(src + c), x1);
+      unpack<T>(ld_stream(src + c + half), x2);
+      unpack<T>(ld_keep(ct + c), cv);
+      unpack<T>(ld_keep(st + c), sv);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        o1[e] = x1[e] * cv[e] - x2[e] * sv[e];
+        o2[e] = x2[e] * cv[e] + x1[e] * sv[e];
+      }
+      st_stream(dst + c, pack<T>(o1));
+      st_stream(dst + c + half, pack<T>(o2));
+    } else {
+      const int c = j * E;  // E elements = E/2 pairs; table entries c/2..
+      float xv[E], o[E];
+      unpack<T>(ld_stream(src + c), xv);
+      const uint2 cw = __ldg(reinterpret_cast<const uint2*>(ct + c / 2));
+      const uint2 sw = __ldg(reinterpret_cast<const uint2*>(st + c / 2));
+      float tmp[E];
+      unpack<T>(make_uint4(cw.x, cw.y, sw.x, sw.y), tmp);
+#pragma unroll
+      for (int i = 0; i < HP; ++i) {
+        const float cc = tmp[i], ss = tmp[HP + i];
+        o[2 * i] = xv[2 * i] * cc - xv[2 * i + 1] * ss;
+        o[2 * i + 1] = xv[2 * i + 1] * cc + xv[2 * i] * ss;
+      }
+      st_stream(dst + c, pack<T>(o));
+    }
+  }
+}
+
+template <typename T, bool INTER>
+__global__ void __launch_bounds__(kRopeThreads) rope_qk_scalar_kernel(const RopeQkArgs a) {
+  const int D = a.D, half = D / 2;
+  const int64_t heads = a.H + a.Hk;
+  const int64_t items = a.B * a.S * heads * half;
+  for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int i = (int)(it % half);
+    const int64_t t = it / half;
+    const int64_t hh = t % heads;
+    const int64_t p = t / heads;
+    const int64_t s = p % a.S;
+    const bool isq = hh < a.H;
+    const int64_t base = isq ? (p * a.H + hh) * D : (p * a.Hk + (hh - a.H)) * D;
+    const T* src = (isq ? static_cast<const T*>(a.q) : static_cast<const T*>(a.k)) + base;
+    T* dst = (isq ? static_cast<T*>(a.qo) : static_cast<T*>(a.ko)) + base;
+    const float c = ld1(static_cast<const T*>(a.cos) + s * half + i);
+    const float sn = ld1(static_cast<const T*>(a.sin) + s * half + i);
+    if (INTER) {
+      const float x1 = ld1(src + 2 * i), x2 = ld1(src + 2 * i + 1);
+      st1(dst + 2 * i, x1 * c - x2 * sn);
+      st1(dst + 2 * i + 1, x2 * c + x1 * sn);
+    } else {
+      const float x1 = ld1(src + i), x2 = ld1(src + i + half);
+      st1(dst + i, x1 * c - x2 * sn);
+      st1(dst + i + half, x2 * c + x1 * sn);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- norm + rope
+struct NormRopeArgs {
+  const void* x;
+  const void* r;
+  const void* w;
+  const void* cos;
+  const void* sin;
+  void* y;
+  int64_t ldx, ldr, ldc, lds, ldy, M;
+  int D;
+  float eps;
+  int aligned;
+};
+
+template <typename T, int V, bool RESID>
+__global__ void __launch_bounds__(256) norm_rope_kernel(const NormRopeArgs a) {
+  constexpr int E = Traits<T>::E;
+  extern __shared__ float nrow[];  // [R][D]
+  __shared__ float red[1024];
+  const Group g;
+  const int64_t row = (int64_t)blockIdx.x * blockDim.y + g.ty;
+  const bool valid = row < a.M;
+  const int D = a.D, half = D / 2;
+  const int N = valid ? D : 0;
+  const T* xr = static_cast<const T*>(a.x) + (valid ? row * a.ldx : 0);
+  float hv[V][E];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * g.G + g.tx) * E;
+    load_vec<T, true>(hv[v], xr, c, N, a.aligned);
+    if (RESID) {
+      float t[E];
+      load_vec<T, true>(t, static_cast<const T*>(a.r) + (valid ? row * a.ldr : 0), c, N, a.aligned);
+#pragma unroll
+      for (int e = 0; e < E; ++e) hv[v][e] += t[e];
+    }
+  }
+  float s = 0.0f;
+#pragma unroll
+  for (int v = 0; v < V; ++v)
+#pragma unroll
+    for (int e = 0; e < E; ++e) s = fmaf(hv[v][e], hv[v][e], s);
+  s = group_sum(s, g, red);
+  const float rs = rsqrtf(s / (float)D + a.eps);
+  float* nr = nrow + (size_t)g.ty * D;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * g.G + g.tx) * E;
+    float wv[E];
+    load_vec<T, false>(wv, static_cast<const T*>(a.w), c, N, a.aligned);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      hv[v][e] = hv[v][e] * rs * wv[e];
+      if (c + e < N) nr[c + e] = hv[v][e];
+    }
+  }
+  __syncthreads();
+  if (!valid) return;
+  const T* cr = static_cast<const T*>(a.cos) + row * a.ldc;
+  const T* sr = static_cast<const T*>(a.sin) + row * a.lds;
+  T* yr = static_cast<T*>(a.y) + row * a.ldy;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * g.G + g.tx) * E;
+    float cv[E], sv[E], o[E];
+    load_vec<T, true>(cv, cr, c, N, a.aligned);
+    load_vec<T, true>(sv, sr, c, N, a.aligned);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int i = c + e;
+      if (i < N) {
+        const float rot = i < half ? -nr[i + half] : nr[i - half];
+        o[e] = hv[v][e] * cv[e] + rot * sv[e];
+      } else {
+        o[e] = 0.0f;
+      }
+    }
+    store_vec<T>(yr, c, N, a.aligned, o);
+  }
+}
+
+static unsigned grid_for(int64_t items) {
+  const int64_t want = (items + kRopeThreads - 1) / kRopeThreads;
+  const int64_t cap = (int64_t)sm_count() * 32;
+  return (unsigned)(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+}  // namespace b2k
+
+using namespace b2k;
+
+extern "C" int b2k_rope(const void* x, int64_t ldx, const void* cos, int64_t ldc, const void* sin,
+                        int64_t lds, void* y, int64_t ldy, int64_t M, int64_t D, int dtype,
+                        int interleaved, void* stream) {
+  B2K_REQUIRE(M >= 0 && D >= 0 && D % 2 == 0, "b2k_rope: need M >= 0 and even D");
+  const int64_t tw = interleaved ? D / 2 : D;
+  B2K_REQUIRE(M <= 1 || (ldx >= D && ldy >= D && ldc >= tw && lds >= tw),
+              "b2k_rope: row stride too small");
+  B2K_REQUIRE(D < (1 << 30), "b2k_rope: D too large");
+  if (M == 0 || D == 0) return B2K_OK;
+  RopeArgs a;
+  a.x = x; a.cos = cos; a.sin = sin; a.y = y;
+  a.ldx = ldx; a.ldc = ldc; a.lds = lds; a.ldy = ldy; a.M = M; a.D = (int)D;
+  const int es = dtype_size(dtype);
+  const int E = es ? 16 / es : 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool rows16 = aligned16(x) && aligned16(y) && (ldx * es) % 16 == 0 && (ldy * es) % 16 == 0;
+  B2K_DISPATCH_FLOAT(dtype, {
+    if (!interleaved) {
+      const bool vec = rows16 && (D / 2) % E == 0 && aligned16(cos) && aligned16(sin) &&
+                       (ldc * es) % 16 == 0 && (lds * es) % 16 == 0;
+      if (vec) {
+        const int vph = (int)(D / 2 / E);
+        const int64_t items = M * vph;
+        rope_half_vec_kernel<T><<<grid_for(items), kRopeThreads, 0, st>>>(a, items, vph);
+      } else {
+        rope_scalar_kernel<T, false><<<grid_for(M * (D / 2)), kRopeThreads, 0, st>>>(a);
+      }
+    } else {
+      const bool vec = rows16 && D % E == 0 && ((uintptr_t)cos % 8 == 0) &&
+                       ((uintptr_t)sin % 8 == 0) && (ldc * es) % 8 == 0 && (lds * es) % 8 == 0;
+      if (vec) {
+        const int vpr = (int)(D / E);
+        const int64_t items = M * vpr;
+        rope_inter_vec_kernel<T><<<grid_for(items), kRopeThreads, 0, st>>>(a, items, vpr);
+      } else {
+        rope_scalar_kernel<T, true><<<grid_for(M * (D / 2)), kRopeThreads, 0, st>>>(a);
+      }
+    }
+    return check_launch("b2k_rope");
+  });
+  return B2K_OK;
+}
+
+extern "C" int b2k_rope_qk(const void* q, const void* k, const void* cos, const void* sin,
+                           void* q_out, void* k_out, int64_t B, int64_t S, int64_t H, int64_t Hk,
+                           int64_t D, int dtype, int interleaved, void* stream) {
+  B2K_REQUIRE(B >= 0 && S >= 0 && H >= 0 && Hk >= 0 && D >= 0 && D % 2 == 0,
+              "b2k_rope_qk: bad shape");
+  B2K_REQUIRE(D < (1 << 20) && H + Hk < (1 << 20), "b2k_rope_qk: shape too large");
+  if (B == 0 || S == 0 || D == 0 || H + Hk == 0) return B2K_OK;
+  RopeQkArgs a;
+  a.q = q; a.k = k; a.cos = cos; a.sin = sin; a.qo = q_out; a.ko = k_out;
+  a.B = B; a.S = S; a.H = H; a.Hk = Hk; a.D = (int)D;
+  const int es = dtype_size(dtype);
+  const int E = es ? 16 / es : 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool base16 = aligned16(q_out) && aligned16(k_out) && (H == 0 || aligned16(q)) &&
+                      (Hk == 0 || aligned16(k)) && (D * es) % 16 == 0;
+  B2K_DISPATCH_FLOAT(dtype, {
+    bool vec;
+    int per_head;
+    if (!interleaved) {
+      vec = base16 && (D / 2) % E == 0 && aligned16(cos) && aligned16(sin) &&
+            ((D / 2) * es) % 16 == 0;
+      per_head = (int)(D / 2 / E);
+    } else {
+      vec = base16 && D % E == 0 && ((uintptr_t)cos % 8 == 0) && ((uintptr_t)sin % 8 == 0) &&
+            ((D / 2) * es) % 8 == 0;
+      per_head = (int)(D / E);
+    }
+    if (vec) {
+      const int64_t items = (H + Hk) * per_head;
+      int threads = (int)((items + 31) / 32 * 32);
+      threads = threads > 1024 ? 1024 : threads;
+      const int64_t grid = B * S;
+      B2K_REQUIRE(grid <= 0x7fffffffLL, "b2k_rope_qk: too many positions");
+      if (interleaved)
+        rope_qk_kernel<T, true><<<(unsigned)grid, threads, 0, st>>>(a, per_head);
+      else
+        rope_qk_kernel<T, false><<<(unsigned)grid, threads, 0, st>>>(a, per_head);
+    } else {
+      const int64_t items = B * S * (H + Hk) * (D / 2);
+      if (interleaved)
+        rope_qk_scalar_kernel<T, true><<<grid_for(items), kRopeThreads, 0, st>>>(a);
+      else
+        rope_qk_scalar_kernel<T, false><<<grid_for(items), kRopeThreads, 0, st>>>(a);
+    }
+    return check_launch("b2k_rope_qk");
+  });
+  return B2K_OK;
+}
+
+extern "C" int b2k_norm_rope(const void* x, int64_t ldx, const void* r, int64_t ldr, const void* w,
+                             const void* cos, int64_t ldc, const void* sin, int64_t lds, void* y,
+                             int64_t ldy, int64_t M, int64_t D, int dtype, float eps,
+                             void* stream) {
+  B2K_REQUIRE(M >= 0 && D >= 0 && D % 2 == 0, "b2k_norm_rope: need M >= 0 and even D");
+  B2K_REQUIRE(M <= 1 || (ldx >= D && ldy >= D && ldc >= D && lds >= D && (!r || ldr >= D)),
+              "b2k_norm_rope: row stride too small");
+  B2K_REQUIRE(D <= 8192, "b2k_norm_rope: head dim above 8192 is not supported");
+  B2K_REQUIRE(w != nullptr, "b2k_norm_rope: weight required");
+  if (M == 0 || D == 0) return B2K_OK;
+  NormRopeArgs a;
+  a.x = x; a.r = r; a.w = w; a.cos = cos; a.sin = sin; a.y = y;
+  a.ldx = ldx; a.ldr = ldr; a.ldc = ldc; a.lds = lds; a.ldy = ldy; a.M = M; a.D = (int)D;
+  a.eps = eps;
+  const int es = dtype_size(dtype);
+  const int E = es ? 16 / es : 1;
+  bool al = D % E == 0 && aligned16(x) && aligned16(y) && aligned16(w) && aligned16(cos) &&
+            aligned16(sin) && (ldx * es) % 16 == 0 && (ldy * es) % 16 == 0 &&
+            (ldc * es) % 16 == 0 && (lds * es) % 16 == 0;
+  if (r) al = al && aligned16(r) && (ldr * es) % 16 == 0;
+  a.aligned = al ? 1 : 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  B2K_DISPATCH_FLOAT(dtype, {
+    RowCfg cfg;
+    if (!choose_row_cfg(D, Traits<T>::E, 32, &cfg, 4, 256)) {
+      set_error("b2k_norm_rope: head dim %lld does not fit", (long long)D);
+      return B2K_EUNSUPPORTED;
+    }
+    const size_t smem = (size_t)cfg.R * D * sizeof(float);
+    const dim3 block(cfg.G, cfg.R);
+    const int64_t grid = (M + cfg.R - 1) / cfg.R;
+    auto go = [&](auto kern) {
+      if (smem > 48 * 1024)
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      kern<<<(unsigned)grid, block, smem, st>>>(a);
+    };
+    if (r) {
+      switch (cfg.V) {
+        case 1: go(norm_rope_kernel<T, 1, true>); break;
+        case 2: go(norm_rope_kernel<T, 2, true>); break;
+        default: go(norm_rope_kernel<T, 4, true>); break;
+      }
+    } else {
+      switch (cfg.V) {
+        case 1: go(norm_rope_kernel<T, 1, false>); break;
+        case 2: go(norm_rope_kernel<T, 2, false>); break;
+        default: go(norm_rope_kernel<T, 4, false>); break;
+      }
+    }
+    return check_launch("b2k_norm_rope");
+  });
+  return B2K_OK;
+}

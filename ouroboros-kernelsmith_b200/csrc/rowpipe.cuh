@@ -1,0 +1,126 @@
+// Persistent row pipeline: a block walks rows first, first+stride, ... and
+// keeps the next S-1 of them streaming into an S-stage shared-memory ring
+// with bulk copies while it computes on the current one.
+//
+// Protocol per row k (stage s = k % S, parity (k / S) & 1):
+//   wait_next()    all threads wait (bounded) for the stage to be full
+//   ...            threads read their slice of the stage, then reach a block
+//                  barrier (every row op here has one in its reduction)
+//   refill()       thread 0 re-arms the stage with row k + S
+// after the loop: drain(k) waits (bounded) for copies still in flight when a
+// wait timed out, so nothing lands in shared memory after the block exits.
+// Inputs are NIN row-major matrices with their own row strides; each row is
+// copied as one bulk transfer of N * sizeof(T) bytes (16-byte multiple).
+#pragma once
+
+#include "tma.cuh"
+
+namespace b2k {
+
+template <int NIN>
+struct RowPipe {
+  unsigned char* dsm;
+  uint64_t* full;
+  int S;
+  uint32_t row_bytes, stage_bytes;
+  int64_t first, stride, nrows, issued;
+  int istage;        // stage of the next issue (issuing thread)
+  int cstage;        // stage of the next row to consume
+  uint32_t cphase;   // its barrier phase parity
+  const unsigned char* src[NIN];
+  int64_t ld_bytes[NIN];
+
+  // dynamic shared memory needed for S stages
+  static size_t smem_bytes(int S, int64_t row_bytes) {
+    return (size_t)S * NIN * (size_t)row_bytes + (size_t)S * sizeof(uint64_t);
+  }
+
+  __device__ __forceinline__ void issue(int64_t k) {
+    const int s = istage;
+    if (++istage == S) istage = 0;
+    const int64_t row = first + k * stride;
+    unsigned char* st = dsm + (size_t)s * stage_bytes;
+    mbar_arrive_expect_tx(&full[s], stage_bytes);
+#pragma unroll
+    for (int i = 0; i < NIN; ++i)
+      bulk_g2s(st + (size_t)i * row_bytes, src[i] + row * ld_bytes[i], row_bytes, &full[s]);
+  }
+
+  // Called by every thread; contains a __syncthreads.
+  __device__ __forceinline__ void init(unsigned char* smem, int stages, int64_t M,
+                                       uint32_t rbytes, const void* const* srcs,
+                                       const int64_t* ld_elems, int elem_bytes) {
+    dsm = smem;
+    S = stages;
+    row_bytes = rbytes;
+    stage_bytes = NIN * rbytes;
+    full = reinterpret_cast<uint64_t*>(dsm + (size_t)S * stage_bytes);
+    first = blockIdx.x;
+    stride = gridDim.x;
+    nrows = first < M ? (M - 1 - first) / stride + 1 : 0;
+#pragma unroll
+    for (int i = 0; i < NIN; ++i) {
+      src[i] = static_cast<const unsigned char*>(srcs[i]);
+      ld_bytes[i] = ld_elems[i] * elem_bytes;
+    }
+    if (threadIdx.x == 0 && threadIdx.y == 0) {
+      for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+      fence_barrier_init();
+    }
+    __syncthreads();
+    issued = 0;
+    istage = 0;
+    cstage = 0;
+    cphase = 0;
+    if (threadIdx.x == 0 && threadIdx.y == 0)
+      for (; issued < nrows && issued < S; ++issued) issue(issued);
+  }
+
+  __device__ __forceinline__ int64_t row_of(int64_t k) const { return first + k * stride; }
+
+  // Bounded wait for the next row (rows are consumed in order 0, 1, ...);
+  // returns the stage base, ok=false on timeout.
+  __device__ __forceinline__ const unsigned char* wait_next(bool& ok) {
+    const int s = cstage;
+    ok = mbar_wait(&full[s], cphase);
+    if (++cstage == S) { cstage = 0; cphase ^= 1u; }
+    return dsm + (size_t)s * stage_bytes;
+  }
+
+  // Thread 0, after a block barrier that follows every thread's reads of the
+  // stage of the row just consumed.
+  __device__ __forceinline__ void refill() {
+    if (threadIdx.x == 0 && threadIdx.y == 0 && issued < nrows) {
+      fence_proxy_async();
+      issue(issued);
+      ++issued;
+    }
+  }
+
+  __device__ __forceinline__ void drain(int64_t k) {
+    if (threadIdx.x == 0 && threadIdx.y == 0)
+      for (int64_t j = k; j < issued; ++j)
+        mbar_wait(&full[(int)(j % S)], (uint32_t)((j / S) & 1));
+  }
+};
+
+// Host: pipeline shape for rows of `stage_bytes` (all inputs of one row).
+// Returns false when the rows do not fit (the caller uses another kernel).
+struct PipeShape {
+  int cps, S;
+};
+
+inline bool choose_pipe_shape(int64_t stage_bytes, int want_cps, int want_stages,
+                              PipeShape* ps) {
+  const int64_t budget = 200 << 10;  // dynamic shared memory per SM
+  int cps = want_cps > 0 ? want_cps : 2;
+  int S = want_stages > 0 ? want_stages : 4;
+  while (S > 2 && (int64_t)cps * S * stage_bytes > budget) --S;
+  while (cps > 1 && (int64_t)cps * S * stage_bytes > budget) --cps;
+  if ((int64_t)cps * S * stage_bytes > budget) return false;
+  ps->cps = cps;
+  ps->S = S;
+  return true;
+}
+
+}  // namespace b2k

@@ -1,0 +1,399 @@
+// Forward cross-entropy (ouroboros/specs.py:239-241): per row
+// loss = logsumexp(x) - x[tgt], 0 for tgt == ignore_index (torch's -100).
+//
+// Rows up to vocabulary size (128256 at the Llama-3 config) are far larger
+// than a block's registers, so each row is streamed once with an online
+// (max, sum-of-exp) pair per thread, merged across the block in one
+// reduction at the end of the row.
+//  * ce_tma_kernel (aligned rows): warp-specialised persistent blocks.  One
+//    producer warp streams the block's rows as 16 KB chunks through an
+//    S-stage shared-memory ring with bulk copies (full/empty mbarriers); the
+//    consumer warps fold each chunk into their running pairs and release the
+//    stage.  Loads never wait for the exponentials and vice versa.
+//  * ce_rows_kernel (any layout): each thread walks its 16-byte vectors U at
+//    a time straight from global memory.  The target logit is a single scalar load; rows whose target is
+// ignore_index are not read at all.  b2k_ce_reduce sums per-row losses of a
+// shard in fp64 in a fixed order (deterministic) and counts valid rows;
+// b2k_ce_mean turns the (possibly all-reduced) pair into the mean.
+#include <stdlib.h>
+
+#include "rowio.cuh"
+#include "tma.cuh"
+
+B2K_DEFINE_TIMEOUT_COUNTER()
+
+namespace b2k {
+
+constexpr int kCeU = 4;
+
+struct CeArgs {
+  const void* x;
+  const int64_t* tgt;
+  void* loss;
+  int64_t ldx, M, N, ignore;
+  int aligned;
+};
+
+template <typename T, typename OutT>
+__global__ void __launch_bounds__(1024) ce_rows_kernel(const CeArgs a) {
+  constexpr int E = Traits<T>::E;
+  constexpr int H = E / 2;
+  constexpr bool P = std::is_same<T, float>::value;
+  __shared__ float red[1024];
+  const Group g;
+  const int64_t row = (int64_t)blockIdx.x * blockDim.y + g.ty;
+  const bool valid = row < a.M;
+  const int64_t N = a.N;
+  const int64_t t = valid ? a.tgt[row] : a.ignore;
+  const bool ignore = (t == a.ignore);
+  const bool bad = !ignore && (t < 0 || t >= N);
+  const T* xr = static_cast<const T*>(a.x) + (valid ? row * a.ldx : 0);
+
+  float m = -INFINITY, s = 0.0f;
+  if (valid && !ignore && !bad) {
+    const int64_t step = (int64_t)g.G * E;
+    for (int64_t c0 = (int64_t)g.tx * E; c0 < N; c0 += step * kCeU) {
+      float2 v[kCeU][H];
+#pragma unroll
+      for (int u = 0; u < kCeU; ++u)
+        load_vec_fill<T, true>(reinterpret_cast<float*>(v[u]), xr, c0 + u * step, N, a.aligned,
+                               -INFINITY);
+      float bm = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < kCeU; ++u)
+#pragma unroll
+        for (int j = 0; j < H; ++j) bm = fmaxf(bm, fmaxf(v[u][j].x, v[u][j].y));
+      const float nm = fmaxf(m, bm);
+      if (nm == -INFINITY) continue;
+      if constexpr (P) {
+        float acc = s * expf(m - nm);
+#pragma unroll
+        for (int u = 0; u < kCeU; ++u)
+#pragma unroll
+          for (int j = 0; j < H; ++j) acc += expf(v[u][j].x - nm) + expf(v[u][j].y - nm);
+        s = acc;
+      } else {
+        const float2 nz = f2s(-nm * kLog2e);
+        float2 acc = f2(s * ex2_approx((m - nm) * kLog2e), 0.0f);
+#pragma unroll
+        for (int u = 0; u < kCeU; ++u)
+#pragma unroll
+          for (int j = 0; j < H; ++j) {
+            const float2 z = fma2(v[u][j], f2s(kLog2e), nz);
+            acc = add2(acc, f2(ex2_approx(z.x), ex2_approx(z.y)));
+          }
+        s = acc.x + acc.y;
+      }
+      m = nm;
+    }
+  }
+  group_lse(m, s, g, red);
+  if (valid && g.tx == 0) {
+    float loss;
+    if (ignore) loss = 0.0f;
+    else if (bad) loss = __int_as_float(0x7fc00000);  // NaN: target outside [0, N)
+    else loss = (m + (P ? logf(s) : f_log<false>(s))) - to_f<T>(xr[t]);
+    static_cast<OutT*>(a.loss)[row] = from_f<OutT>(loss);
+  }
+}
+
+constexpr int kCeChunkBytes = 16384;
+constexpr int kCeConsumerWarps = 8;
+constexpr int kCeThreads = 32 * (kCeConsumerWarps + 1);
+
+template <typename T, typename OutT>
+__global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, const int S) {
+  constexpr int E = Traits<T>::E;
+  constexpr int H = E / 2;
+  constexpr bool P = std::is_same<T, float>::value;
+  constexpr int NC = 32 * kCeConsumerWarps;           // consumer threads
+  constexpr int CE = kCeChunkBytes / (int)sizeof(T);  // elements per chunk
+  constexpr int VPT = CE / E / NC;                    // vectors per consumer per chunk
+  static_assert(VPT * E * NC == CE, "chunk must split evenly over the consumers");
+  extern __shared__ __align__(128) unsigned char dsm[];
+  __shared__ float red_m[kCeConsumerWarps], red_s[kCeConsumerWarps];
+  __shared__ volatile int abort_flag;
+  __shared__ int stop;
+  __shared__ int64_t consumed;
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + (size_t)S * kCeChunkBytes);
+  uint64_t* empty = full + S;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t first = blockIdx.x, stride = gridDim.x;
+  const int64_t nrows = first < a.M ? (a.M - 1 - first) / stride + 1 : 0;
+  const int64_t N = a.N;
+  const int64_t nchunks = (N + CE - 1) / CE;
+  const T* xg = static_cast<const T*>(a.x);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kCeConsumerWarps);
+    }
+    fence_barrier_init();
+    abort_flag = 0;
+    stop = 0;
+    consumed = 0;
+  }
+  __syncthreads();
+
+  int64_t issued = 0;
+  // ring position as (stage, phase) counters: no 64-bit division per chunk
+  int p_stage = 0;
+  uint32_t p_phase = 0;  // phase of the current lap; the empty wait is for the previous lap
+  if (warp == 0) {
+    // ---- producer warp: the whole warp walks the loop (warp-uniform
+    // control flow), lane 0 issues the bulk copies
+    for (int64_t i = 0; i < nrows; ++i) {
+      if (__any_sync(0xffffffffu, abort_flag != 0)) break;
+      const int64_t row = first + i * stride;
+      const int64_t t = a.tgt[row];
+      if (t == a.ignore || t < 0 || t >= N) continue;
+      const T* xr = xg + row * a.ldx;
+      bool ok = true;
+      for (int64_t c = 0; c < nchunks; ++c) {
+        const int s = p_stage;
+        if (issued >= S) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], p_phase ^ 1u));
+          if (!ok) {
+            if (lane == 0) { abort_flag = 1; atomicAdd(&b2k_tu_timeouts, 1u); }
+            break;
+          }
+        }
+        if (lane == 0) {
+          const int64_t n = (N - c * CE) < CE ? (N - c * CE) : CE;
+          const uint32_t bytes = (uint32_t)(n * (int64_t)sizeof(T));
+          mbar_arrive_expect_tx(&full[s], bytes);
+          bulk_g2s(dsm + (size_t)s * kCeChunkBytes, xr + c * CE, bytes, &full[s]);
+        }
+        ++issued;
+        if (++p_stage == S) { p_stage = 0; p_phase ^= 1u; }
+      }
+      __syncwarp();
+      if (!ok) break;
+    }
+  } else {
+    // ---- consumers
+    const int ct = threadIdx.x - 32;
+    const int cw = warp - 1;
+    int64_t u = 0;
+    int c_stage = 0;
+    uint32_t c_phase = 0;
+    for (int64_t i = 0; i < nrows; ++i) {
+      const int64_t row = first + i * stride;
+      const int64_t t = a.tgt[row];
+      const bool ignore = (t == a.ignore);
+      if (ignore || t < 0 || t >= N) {
+        if (ct == 0)
+          static_cast<OutT*>(a.loss)[row] =
+              from_f<OutT>(ignore ? 0.0f : __int_as_float(0x7fc00000));
+        continue;
+      }
+      float m = -INFINITY, s = 0.0f;
+      int n_left = (int)(N < (int64_t)0x7fffffff ? N : 0x7fffffff);
+      for (int64_t c = 0; c < nchunks; ++c, ++u, n_left -= CE) {
+        const int st = c_stage;
+        bool ok = false;
+        if (!abort_flag) {
+          ok = mbar_wait(&full[st], c_phase);
+          if (!ok) { abort_flag = 1; atomicAdd(&b2k_tu_timeouts, 1u); }
+        }
+        if (ok) {
+          const T* cs = reinterpret_cast<const T*>(dsm + (size_t)st * kCeChunkBytes);
+          const int n = n_left < CE ? n_left : CE;
+          float2 v[VPT][H];
+#pragma unroll
+          for (int k = 0; k < VPT; ++k) {
+            const int idx = (k * NC + ct) * E;
+            if (idx < n) {
+              unpack2<T>(*reinterpret_cast<const uint4*>(cs + idx), v[k]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < H; ++j) v[k][j] = f2s(-INFINITY);
+            }
+          }
+          // tree max (short dependency chains)
+          float bmk[VPT];
+#pragma unroll
+          for (int k = 0; k < VPT; ++k) {
+            float t0 = fmaxf(v[k][0].x, v[k][0].y);
+#pragma unroll
+            for (int j = 1; j < H; ++j) t0 = fmaxf(t0, fmaxf(v[k][j].x, v[k][j].y));
+            bmk[k] = t0;
+          }
+          float bm = bmk[0];
+#pragma unroll
+          for (int k = 1; k < VPT; ++k) bm = fmaxf(bm, bmk[k]);
+          const float nm = fmaxf(m, bm);
+          if (nm != -INFINITY) {
+            if constexpr (P) {
+              float acc = s * expf(m - nm);
+#pragma unroll
+              for (int k = 0; k < VPT; ++k)
+#pragma unroll
+                for (int j = 0; j < H; ++j) acc += expf(v[k][j].x - nm) + expf(v[k][j].y - nm);
+              s = acc;
+            } else {
+              const float2 nz = f2s(-nm * kLog2e);
+              float2 acc[VPT];
+#pragma unroll
+              for (int k = 0; k < VPT; ++k) {
+                acc[k] = f2s(0.0f);
+#pragma unroll
+                for (int j = 0; j < H; ++j) {
+                  const float2 z = fma2(v[k][j], f2s(kLog2e), nz);
+                  acc[k] = add2(acc[k], f2(ex2_approx(z.x), ex2_approx(z.y)));
+                }
+              }
+#pragma unroll
+              for (int k = 1; k < VPT; ++k) acc[0] = add2(acc[0], acc[k]);
+              s = fmaf(s, ex2_approx((m - nm) * kLog2e), acc[0].x + acc[0].y);
+            }
+            m = nm;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        if (++c_stage == S) { c_stage = 0; c_phase ^= 1u; }
+      }
+      // merge the consumers' pairs: warp shuffles, then across warps
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+        lse_merge(m, s, m2, s2);
+      }
+      if (lane == 0) { red_m[cw] = m; red_s[cw] = s; }
+      named_bar_sync(1, NC);
+      if (ct == 0) {
+        float M = red_m[0], Ssum = red_s[0];
+        for (int w = 1; w < kCeConsumerWarps; ++w) lse_merge(M, Ssum, red_m[w], red_s[w]);
+        const float lse = M + (P ? logf(Ssum) : f_log<false>(Ssum));
+        const float xt = to_f<T>(xg[row * a.ldx + t]);
+        static_cast<OutT*>(a.loss)[row] = from_f<OutT>(lse - xt);
+        stop = abort_flag;
+      }
+      named_bar_sync(1, NC);
+      if (stop) break;
+    }
+    if (ct == 0) consumed = u;
+  }
+  __syncthreads();
+  // after an abort, wait (bounded) for copies still in flight
+  if (threadIdx.x == 0)
+    for (int64_t j = consumed; j < issued; ++j)
+      mbar_wait(&full[(int)(j % S)], (uint32_t)((j / S) & 1));
+}
+
+static int ce_env(const char* name, int dflt) {
+  const char* s = getenv(name);
+  return s ? atoi(s) : dflt;
+}
+
+template <typename T, typename OutT>
+static int ce_launch(const CeArgs& a, cudaStream_t st) {
+  constexpr int E = Traits<T>::E;
+  static const int use_tma = ce_env("B2K_TMA", 1);
+  if (use_tma && a.aligned && a.N * (int64_t)sizeof(T) >= 4 * kCeChunkBytes) {
+    static const int S = [] {
+      const int v = ce_env("B2K_CE_STAGES", 4);
+      return v >= 2 && v <= 12 ? v : 4;
+    }();
+    static const int cps = [] {
+      const int v = ce_env("B2K_CE_CPS", 3);
+      return v >= 1 && v <= 4 ? v : 3;
+    }();
+    const size_t smem = (size_t)S * kCeChunkBytes + 2 * (size_t)S * sizeof(uint64_t);
+    int64_t grid = (int64_t)sm_count() * cps;
+    if (grid > a.M) grid = a.M;
+    cudaFuncSetAttribute(ce_tma_kernel<T, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    ce_tma_kernel<T, OutT><<<(unsigned)grid, kCeThreads, smem, st>>>(a, S);
+    return check_launch("b2k_cross_entropy(tma)");
+  }
+  const int64_t nvec = (a.N + E - 1) / E;
+  // threads per row: enough that each walks ~32 vectors, 32..1024
+  int G = next_pow2((nvec + 31) / 32);
+  G = G < 32 ? 32 : (G > 1024 ? 1024 : G);
+  static const int override_g = [] {
+    const char* s = getenv("B2K_CE_THREADS");
+    const int v = s ? atoi(s) : 0;
+    return (v >= 32 && v <= 1024 && (v & (v - 1)) == 0) ? v : 0;
+  }();
+  if (override_g) G = override_g;
+  const int R = G >= 256 ? 1 : 256 / G;
+  const int64_t grid = (a.M + R - 1) / R;
+  ce_rows_kernel<T, OutT><<<(unsigned)grid, dim3(G, R), 0, st>>>(a);
+  return check_launch("b2k_cross_entropy");
+}
+
+// one block, fixed summation order
+__global__ void __launch_bounds__(1024) ce_reduce_kernel(const float* loss, const int64_t* tgt,
+                                                         int64_t M, int64_t ignore,
+                                                         double* sumcount) {
+  __shared__ double rs[32], rc[32];
+  double s = 0.0, c = 0.0;
+  for (int64_t i = threadIdx.x; i < M; i += blockDim.x) {
+    if (tgt[i] != ignore) { s += (double)loss[i]; c += 1.0; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    c += __shfl_xor_sync(0xffffffffu, c, o);
+  }
+  if ((threadIdx.x & 31) == 0) { rs[threadIdx.x >> 5] = s; rc[threadIdx.x >> 5] = c; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double ts = 0.0, tc = 0.0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) { ts += rs[i]; tc += rc[i]; }
+    sumcount[0] = ts;
+    sumcount[1] = tc;
+  }
+}
+
+__global__ void ce_mean_kernel(const double* sumcount, float* out) {
+  out[0] = (float)(sumcount[0] / sumcount[1]);  // 0/0 -> NaN (no valid row)
+}
+
+}  // namespace b2k
+
+using namespace b2k;
+
+extern "C" int b2k_cross_entropy(const void* x, int64_t ldx, const int64_t* tgt, void* loss,
+                                 int64_t M, int64_t N, int dtype, int out_dtype,
+                                 int64_t ignore_index, void* stream) {
+  B2K_REQUIRE(M >= 0 && N >= 0, "b2k_cross_entropy: negative shape");
+  B2K_REQUIRE(M <= 1 || ldx >= N, "b2k_cross_entropy: row stride smaller than N");
+  B2K_REQUIRE(M <= 0x7fffffffLL * 8LL, "b2k_cross_entropy: too many rows");
+  B2K_REQUIRE(out_dtype == dtype || out_dtype == B2K_F32,
+              "b2k_cross_entropy: out_dtype must be the input dtype or F32");
+  if (M == 0) return B2K_OK;
+  B2K_REQUIRE(x != nullptr || N == 0, "b2k_cross_entropy: null x");
+  B2K_REQUIRE(tgt != nullptr && loss != nullptr, "b2k_cross_entropy: null tgt/loss");
+  CeArgs a;
+  a.x = x; a.tgt = tgt; a.loss = loss; a.ldx = ldx; a.M = M; a.N = N; a.ignore = ignore_index;
+  const int es = dtype_size(dtype);
+  const int E = es ? 16 / es : 1;
+  a.aligned = (N % E == 0) && aligned16(x) && ((ldx * es) % 16 == 0);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  B2K_DISPATCH_FLOAT(dtype, {
+    if (out_dtype == B2K_F32) return ce_launch<T, float>(a, st);
+    return ce_launch<T, T>(a, st);
+  });
+  return B2K_OK;
+}
+
+extern "C" int b2k_ce_reduce(const float* row_loss, const int64_t* tgt, int64_t M,
+                             int64_t ignore_index, double* sumcount, void* stream) {
+  B2K_REQUIRE(M >= 0, "b2k_ce_reduce: negative M");
+  B2K_REQUIRE(sumcount != nullptr, "b2k_ce_reduce: null output");
+  B2K_REQUIRE(M == 0 || (row_loss != nullptr && tgt != nullptr), "b2k_ce_reduce: null input");
+  ce_reduce_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(row_loss, tgt, M,
+                                                                    ignore_index, sumcount);
+  return check_launch("b2k_ce_reduce");
+}
+
+extern "C" int b2k_ce_mean(const double* sumcount, float* out, void* stream) {
+  B2K_REQUIRE(sumcount != nullptr && out != nullptr, "b2k_ce_mean: null pointer");
+  ce_mean_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(sumcount, out);
+  return check_launch("b2k_ce_mean");
+}

@@ -118,6 +118,10 @@ def main():
     if args.ops:
         ops = args.ops.split(",")
     manifest = {}
+    mpath = os.path.join(HERE, "manifest.json")
+    if args.ops and os.path.exists(mpath):  # partial regeneration keeps the rest
+        with open(mpath) as f:
+            manifest = json.load(f)["ops"]
     for op in ops:
         ref = specs.SPECS[op].reference
         arrays = {}
@@ -133,8 +137,17 @@ def main():
         np.savez_compressed(os.path.join(HERE, f"{op}.npz"), **arrays)
         manifest[op] = len(recs)
         print(f"{op}: {len(recs)} cases")
-    with open(os.path.join(HERE, "manifest.json"), "w") as f:
-        json.dump({"ops": manifest, "torch": torch.__version__,
+    # run() argument names per op, from the spec's signature hint (the
+    # drop-in contract: same inputs in the same order)
+    import re
+    sigs = {}
+    for name, spec in specs.SPECS.items():
+        m = re.search(r"def run\(([^)]*)\)", spec.signature_hint)
+        sigs[name] = [a.strip() for a in m.group(1).split(",")] if m else None
+    with open(os.path.join(HERE, "signatures.json"), "w") as f:
+        json.dump(sigs, f, indent=0, sort_keys=True)
+    with open(mpath, "w") as f:
+        json.dump({"ops": dict(sorted(manifest.items())), "torch": torch.__version__,
                    "source": "ouroboros/specs.py SPECS[op].reference on CPU"}, f, indent=1)
 
 

@@ -1,0 +1,194 @@
+"""GPU parity beyond the spec cases: attention-layout RoPE, the reduced
+cross-entropy, the fused residual-stream output, strided and misaligned
+views (scalar kernel paths), edge shapes, long rows (streaming kernels),
+and the harness import path of a generated candidate."""
+import importlib.util
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import b200k
+from b200k import _lib, registry
+from gpu_util import TDT, to_cuda
+from oracle import ops as O
+from oracle import regimes
+from oracle.numerics import allclose_report, rnd, tol_for
+
+pytestmark = pytest.mark.gpu
+DTS = ["f16", "bf16", "f32"]
+
+
+def _close(out, ref, dt, op="x"):
+    ok, err, bad = allclose_report(out.float().cpu().numpy(), ref, *tol_for(op, dt))
+    assert ok, f"max err {err}, {bad} bad"
+
+
+def _randn(shape, dt, scale, seed):
+    g = np.random.default_rng(seed)
+    return rnd(g.standard_normal(shape, dtype=np.float32) * np.float32(scale), dt)
+
+
+def _t(a, dt):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda().to(TDT[dt])
+
+
+# ---------------------------------------------------------------- rope_qk
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("inter", [False, True])
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_rope_qk_small(dt, inter, D):
+    B, S, H, Hk = 2, 33, 4, 2
+    q = _randn((B, S, H, D), dt, 4.0, 1)
+    k = _randn((B, S, Hk, D), dt, 4.0, 2)
+    ang = np.arange(S, dtype=np.float32)[:, None] * (
+        10000.0 ** (-np.arange(0, D, 2, dtype=np.float32) / D))[None, :]
+    c, s = rnd(np.cos(ang), dt), rnd(np.sin(ang), dt)
+    qo, ko = b200k.rope_qk(_t(q, dt), _t(k, dt), _t(c, dt), _t(s, dt), interleaved=inter)
+    torch.cuda.synchronize()
+    rq, rk = O.rope_qk_tables(q, k, c, s, dt, interleaved=inter)
+    _close(qo, rq, dt)
+    _close(ko, rk, dt)
+
+
+@pytest.mark.parametrize("inter", [False, True])
+def test_rope_qk_llama_shape_sampled(inter):
+    """q [8,4096,32,128], k [8,4096,8,128] bf16; positions sampled."""
+    B, S, H, Hk, D = 8, 4096, 32, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn((B, S, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn((B, S, Hk, D), generator=g, device="cuda").to(torch.bfloat16)
+    inv = 10000.0 ** (-torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D)
+    ang = torch.arange(S, device="cuda", dtype=torch.float32)[:, None] * inv[None, :]
+    c, s = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    qo, ko = b200k.rope_qk(q, k, c, s, interleaved=inter)
+    torch.cuda.synchronize()
+    bs = [0, 3, 7]
+    ss = [0, 1, 2047, 4095]
+    for b in bs:
+        qn = q[b, ss].float().cpu().numpy()[None]
+        kn = k[b, ss].float().cpu().numpy()[None]
+        rq, rk = O.rope_qk_tables(qn, kn, c[ss].float().cpu().numpy(), s[ss].float().cpu().numpy(),
+                                  "bf16", interleaved=inter)
+        _close(qo[b, ss][None], rq, "bf16")
+        _close(ko[b, ss][None], rk, "bf16")
+
+
+# ---------------------------------------------------------------- reduced CE
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("shape", [(37, 4097), (256, 32000), (64, 128256)])
+def test_cross_entropy_mean(dt, shape):
+    M, V = shape
+    case = regimes.make_case("ce", 11, M, V, dt, 3.0, ignore_frac=0.05)
+    x, t = to_cuda(case)
+    got = float(b200k.cross_entropy_mean(x, t))
+    s, c = O.cross_entropy_sum_count(case[0][0], case[1][0].astype(np.int64))
+    want = s / c
+    assert abs(got - want) <= 1e-3 * abs(want), (got, want)
+
+
+def test_cross_entropy_edge_targets():
+    x = _t(_randn((4, 300), "f32", 3.0, 5), "f32")
+    t = torch.tensor([5, -100, 299, 300], device="cuda", dtype=torch.int64)
+    out = b200k.cross_entropy(x, t).cpu().numpy()
+    ref = O.cross_entropy(x.cpu().numpy()[:3], t.cpu().numpy()[:3], "f32")
+    assert np.allclose(out[:3], ref, rtol=2e-4, atol=2e-5)
+    assert out[1] == 0.0
+    assert np.isnan(out[3])  # target outside [0, V) and not ignore_index
+    allign = torch.full((4,), -100, device="cuda", dtype=torch.int64)
+    assert np.isnan(float(b200k.cross_entropy_mean(x, allign)))
+
+
+# ---------------------------------------------------------------- residual stream
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("norm", ["layer", "rms"])
+@pytest.mark.parametrize("N", [8192, 4097, 1024])
+def test_fused_add_norm(dt, norm, N):
+    M = 19
+    x, r = _randn((M, N), dt, 8.0, 1), _randn((M, N), dt, 8.0, 2)
+    w, b = _randn((N,), dt, 1.0, 3), _randn((N,), dt, 1.0, 4)
+    h, y = b200k.fused_add_norm(_t(x, dt), _t(r, dt), _t(w, dt), _t(b, dt), norm=norm,
+                                act="gelu")
+    torch.cuda.synchronize()
+    assert np.array_equal(h.float().cpu().numpy(), rnd(x + r, dt))
+    args = [x, r, w, b] if norm == "layer" else [x, r, w]
+    _close(y, O.chain(norm, True, "gelu", args, dt), dt)
+
+
+# ---------------------------------------------------------------- views
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("op", ["rmsnorm", "add_layernorm_silu", "softmax", "log_softmax",
+                                "swiglu", "gelu", "cross_entropy", "cumsum", "entropy", "kl_div",
+                                "rope", "rope_interleaved"])
+@pytest.mark.parametrize("view", ["strided", "offset"])
+def test_non_contiguous_views(dt, op, view):
+    """Row-strided views and bases shifted by one element (16-byte alignment
+    lost) must give the same results through the scalar paths."""
+    info = regimes.OPS[op]
+    N = 64 if "rope" in op else 2048
+    case = regimes.make_case(info.kind, 21, 9, N, dt, 8.0)
+    base = to_cuda(case)
+    args = []
+    for (v, tag), t in zip(case, base):
+        if t.dim() == 2 and t.shape[0] == 9 and t.is_floating_point():
+            if view == "strided":
+                big = torch.zeros((9, t.shape[1] + 24), dtype=t.dtype, device="cuda")
+                big[:, 8:8 + t.shape[1]] = t
+                t = big[:, 8:8 + t.shape[1]]
+            else:
+                flat = torch.zeros(t.numel() + 1, dtype=t.dtype, device="cuda")
+                flat[1:] = t.reshape(-1)
+                t = flat[1:].view(t.shape)
+        args.append(t)
+    out = b200k.get_op(op)(*args)
+    torch.cuda.synchronize()
+    _close(out, regimes.reference(op, case), dt, op)
+
+
+# ---------------------------------------------------------------- shapes
+@pytest.mark.parametrize("op", ["rmsnorm", "layernorm_gelu", "softmax", "softcap_softmax",
+                                "entropy", "kl_div", "cumsum", "cross_entropy", "l2norm"])
+@pytest.mark.parametrize("N", [1, 2, 3, 70000])
+def test_edge_and_long_rows(op, N):
+    info = regimes.OPS[op]
+    dt = "bf16"
+    case = regimes.make_case(info.kind, 31, 3, N, dt, 4.0)
+    out = b200k.get_op(op)(*to_cuda(case))
+    torch.cuda.synchronize()
+    _close(out, regimes.reference(op, case), dt, op)
+
+
+def test_empty_inputs():
+    x = torch.empty((0, 64), device="cuda", dtype=torch.float16)
+    w = torch.ones(64, device="cuda", dtype=torch.float16)
+    assert b200k.rmsnorm(x, w).shape == (0, 64)
+    assert b200k.softmax(x).shape == (0, 64)
+    assert b200k.swiglu(x, x).shape == (0, 64)
+
+
+# ---------------------------------------------------------------- drop-in
+def test_candidate_imports_like_the_harness(tmp_path):
+    """Write a generated candidate to a file and import it the way
+    ouroboros/harness.py:135-148 does (preamble + source, `run` attribute),
+    then apply the harness contract: fresh output, inputs untouched, and a
+    poked input changes the next result (no memoisation)."""
+    pkg = os.path.dirname(os.path.dirname(b200k.__file__))
+    src = "import torch\n\n" + registry.candidate_source("softmax", pkg)
+    path = tmp_path / "cand_softmax.py"
+    path.write_text(src)
+    spec = importlib.util.spec_from_file_location("cand_softmax", str(path))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    case = regimes.stress_cases("softmax")[0]
+    (x,) = to_cuda(case)
+    clone = x.clone()
+    y1 = mod.run(clone)
+    assert torch.equal(clone, x) and y1.data_ptr() != clone.data_ptr()
+    clone.view(-1)[0] = 1000.0  # dominates row 0 at any stress magnitude
+    y2 = mod.run(clone)
+    ref = O.softmax(clone.float().cpu().numpy(), "f16")
+    _close(y2, ref, "f16")
+    assert not torch.equal(y1, y2)
+    torch.cuda.synchronize()
+    assert _lib.lib.b2k_pipeline_timeouts(1) == 0

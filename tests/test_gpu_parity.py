@@ -3,6 +3,8 @@ reference itself) and with the CPU oracle on the harness's case mix: the
 deterministic stress cases, the bench shape and the adversarial random sweep
 (ouroboros/harness.py:166-202).  Every call goes through the C ABI
 (libb200k.so) via the b200k spec-signature functions."""
+import zlib
+
 import numpy as np
 import pytest
 import torch
@@ -41,7 +43,7 @@ def test_golden(op):
 def test_stress_and_random(op):
     _require(op)
     run = b200k.get_op(op)
-    cases = regimes.stress_cases(op) + regimes.random_cases(op, 6, seed=hash(op) & 0xffff,
+    cases = regimes.stress_cases(op) + regimes.random_cases(op, 6, seed=zlib.crc32(op.encode()),
                                                             max_elems=1 << 20)
     for case in cases:
         ref = regimes.reference(op, case)
