@@ -186,6 +186,24 @@ int b2k_ce_reduce(const float* row_loss, const int64_t* tgt, int64_t M,
 /* out[0] = (float)(sumcount[0] / sumcount[1]) (NaN when the count is 0). */
 int b2k_ce_mean(const double* sumcount, float* out, void* stream);
 
+/* Largest M accepted by b2k_cross_entropy_mean_noalloc. */
+#define B2K_NOALLOC_MAX_ROWS 262144
+
+/* Mean cross-entropy over rows whose target is not ignore_index, written to
+ * out[0] (fp32, device memory), for callers that cannot allocate device
+ * memory: the same result as b2k_cross_entropy(out_dtype F32) ->
+ * b2k_ce_reduce -> b2k_ce_mean, but the per-row losses and the [sum, count]
+ * pair live in a fixed buffer inside the library (1 MiB + 256 B on every GPU
+ * that loads it), so the caller passes only inputs and the output and
+ * nothing is allocated.  M above B2K_NOALLOC_MAX_ROWS is rejected with
+ * B2K_EINVAL.  The first call on a device looks up the buffer's device
+ * address (make it before any stream capture); calls whose GPU work overlaps
+ * share the buffer and race.  No counterpart in the reference: its kernels
+ * allocate their outputs through PyTorch. */
+int b2k_cross_entropy_mean_noalloc(const void* x, int64_t ldx, const int64_t* tgt,
+                                   int64_t M, int64_t N, int dtype,
+                                   int64_t ignore_index, float* out, void* stream);
+
 /* Row-wise inclusive prefix sum, fp64 carry, output in dtype.
  * Replaces cumsum (specs.py:840-849, reference :245-248). */
 int b2k_cumsum(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M,

@@ -53,6 +53,8 @@ SIGNATURES = {
                                   c_int, c_int64, c_void_p]),
     "b2k_ce_reduce": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
     "b2k_ce_mean": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "b2k_cross_entropy_mean_noalloc": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64,
+                                               c_int, c_int64, c_void_p, c_void_p]),
     "b2k_cumsum": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int,
                            c_void_p]),
     "b2k_entropy": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_void_p]),
