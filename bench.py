@@ -11,7 +11,7 @@ Workloads (synthetic data of the named shapes, seeded per rank):
             x, r [16384, 8192], outputs (h = x + r, y), eps 1e-5
   rmsnorm   x [4096, 4096] fp16, w = 1 + 0.1 N(0,1), eps 1e-6
   swiglu    gate, up [8192, 14336] bf16, N(0,1)*2
-  rope      q [8,4096,32,128], k [8,4096,8,128] bf16, tables [4096, 64]
+  rope      q [8,4096,32,128], k [8,4096,8,128] bf16, tables [4096, 64] (neox)
   rope_interleaved   same shapes, GPT-J pairs
   ce        logits [32768, 128256] bf16, N(0,1)*3, 5% targets = -100,
             mean loss over valid rows (rows split across ranks, NCCL
@@ -125,6 +125,10 @@ class Workload:
     scaling = "weak"
     dtype = "bf16"
     launches_per_step = 1
+    graph_steps = 0  # > 0: time from a CUDA graph of this many steps (launch-bound sizes)
+
+    def e2e_api(self):
+        return "b200k.host.run_rows_host (pinned host buffers, copies overlapped with kernels)"
 
     def setup(self, device, rank, world): ...
     def step(self): ...
@@ -162,6 +166,15 @@ class Chain(Workload):
         return {"workload": "add_layernorm_gelu_tanh_h_y", "M": self.M, "N": self.N,
                 "outputs": "h=x+r, y=gelu_tanh(LN(h)*g+b)", "eps": 1e-5,
                 "l2": "inputs exceed L2 (1 GiB working set per step)"}
+
+    def eager_step(self):
+        # ouroboros/chains.py:69-87 (add_layernorm_gelu) in torch eager, plus h
+        hf = self.x.float() + self.r.float()
+        mu = hf.mean(-1, keepdim=True)
+        hc = hf - mu
+        n = hc * torch.rsqrt((hc * hc).mean(-1, keepdim=True) + 1e-5) * self.w.float() + self.b.float()
+        y = (0.5 * n * (1.0 + torch.tanh(0.7978845608028654 * (n + 0.044715 * n * n * n))))
+        return hf.to(torch.bfloat16), y.to(torch.bfloat16)
 
     def e2e_setup(self):
         self.hx = self.x.cpu().pin_memory()
@@ -207,6 +220,7 @@ class RMSNorm(Workload):
     dtype = "fp16"
     M = N = 4096
     SETS = 8
+    graph_steps = 8
 
     def setup(self, device, rank, world):
         import b200k
@@ -224,6 +238,12 @@ class RMSNorm(Workload):
 
     def bytes_per_step(self):
         return 2 * self.M * self.N * 2 + self.N * 2
+
+    def eager_step(self):
+        x = self.xs[self.i % self.SETS]
+        self.i += 1
+        xf = x.float()  # ouroboros/specs.py:75-78
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype) * self.w
 
     def config(self):
         return {"workload": "rmsnorm", "M": self.M, "N": self.N, "eps": 1e-6,
@@ -274,6 +294,9 @@ class SwiGLU(Workload):
 
     def bytes_per_step(self):
         return 3 * self.M * self.N * 2
+
+    def eager_step(self):  # ouroboros/specs.py:85-87
+        return (torch.nn.functional.silu(self.g.float()) * self.u.float()).to(self.g.dtype)
 
     def config(self):
         return {"workload": "swiglu", "M": self.M, "N": self.N,
@@ -346,6 +369,10 @@ class CrossEntropy(Workload):
         rows = self.r1 - self.r0
         return rows * self.V * 2 + rows * 8
 
+    def eager_step(self):
+        # ouroboros/specs.py:239-241 reduced to the mean over valid rows
+        return torch.nn.functional.cross_entropy(self.x.float(), self.t, ignore_index=-100)
+
     def config(self):
         return {"workload": "cross_entropy_mean", "T": self.T, "V": self.V,
                 "ignore_index": -100, "ignore_frac": 0.05,
@@ -362,6 +389,10 @@ class CrossEntropy(Workload):
 
     def e2e_bytes(self):
         return self.e2e_rows * (self.V * 2 + 8)
+
+    def e2e_api(self):
+        return ("b200k.cross_entropy_mean on a 4096-row slice copied from pinned host memory, "
+                "fp32 mean copied back")
 
     def e2e_step(self, timing):
         cur = torch.cuda.current_stream(self.device)
@@ -389,7 +420,134 @@ class CrossEntropy(Workload):
         return self.V * 2 + 8
 
 
-WORKLOADS = {"chain": Chain, "rmsnorm": RMSNorm, "swiglu": SwiGLU, "ce": CrossEntropy}
+class RoPE(Workload):
+    """q [8,4096,32,128], k [8,4096,8,128] bf16, positions 0..S-1,
+    theta 10000, tables [S, 64] computed in fp32 and cast to bf16; q and k
+    rotated in one launch into fresh outputs."""
+    name = "rope_qk"
+    B, S, H, Hk, D = 8, 4096, 32, 8, 128
+    interleaved = False
+
+    def setup(self, device, rank, world):
+        import b200k
+        self.b2k = b200k
+        s = 1000 * rank
+        self.q = _randn((self.B, self.S, self.H, self.D), torch.bfloat16, device, s + 31)
+        self.k = _randn((self.B, self.S, self.Hk, self.D), torch.bfloat16, device, s + 32)
+        inv = 10000.0 ** (-torch.arange(0, self.D, 2, device=device, dtype=torch.float32) / self.D)
+        ang = torch.arange(self.S, device=device, dtype=torch.float32)[:, None] * inv[None, :]
+        self.cos = ang.cos().to(torch.bfloat16)
+        self.sin = ang.sin().to(torch.bfloat16)
+        self.device = device
+
+    def step(self):
+        return self.b2k.rope_qk(self.q, self.k, self.cos, self.sin, interleaved=self.interleaved)
+
+    def bytes_per_step(self):
+        qk = (self.B * self.S * (self.H + self.Hk) * self.D) * 2
+        return 2 * qk + 2 * self.S * (self.D // 2) * 2
+
+    def eager_step(self):
+        # ouroboros/specs.py:96-102 / :228-236 with the tables broadcast over heads
+        c = self.cos.float()[None, :, None, :]
+        s = self.sin.float()[None, :, None, :]
+        out = []
+        for t in (self.q, self.k):
+            tf = t.float()
+            if self.interleaved:
+                o = torch.empty_like(tf)
+                o[..., 0::2] = tf[..., 0::2] * c - tf[..., 1::2] * s
+                o[..., 1::2] = tf[..., 1::2] * c + tf[..., 0::2] * s
+            else:
+                h = self.D // 2
+                rot = torch.cat([-tf[..., h:], tf[..., :h]], dim=-1)
+                o = tf * torch.cat([c, c], -1) + rot * torch.cat([s, s], -1)
+            out.append(o.to(t.dtype))
+        return tuple(out)
+
+    def config(self):
+        return {"workload": "rope_qk_interleaved" if self.interleaved else "rope_qk_neox",
+                "q": [self.B, self.S, self.H, self.D], "k": [self.B, self.S, self.Hk, self.D],
+                "tables": [self.S, self.D // 2], "theta": 10000.0,
+                "l2": "inputs exceed L2 (336 MB read per step)"}
+
+    def e2e_setup(self):
+        self.hq = self.q.cpu().pin_memory()
+        self.hk = self.k.cpu().pin_memory()
+        self.hc, self.hs = self.cos.cpu(), self.sin.cpu()
+        self.hqo = torch.empty_like(self.hq).pin_memory()
+        self.hko = torch.empty_like(self.hk).pin_memory()
+        qk = (self.B * self.S * (self.H + self.Hk) * self.D) * 2
+        return (qk + 2 * self.S * (self.D // 2) * 2, qk)
+
+    def e2e_step(self, timing):
+        from b200k.host import run_rows_host
+        b2k, inter = self.b2k, self.interleaved
+        run_rows_host(lambda q, k, c, s: b2k.rope_qk(q, k, c, s, interleaved=inter),
+                      [self.hq, self.hk], [self.hc, self.hs], out=(self.hqo, self.hko),
+                      device=self.device, timing=timing)
+
+    def cpu_prepare(self):
+        from oracle.numerics import bf16_round
+        g = np.random.default_rng(0)
+        self.cq = bf16_round(g.standard_normal((1, self.S, self.H, self.D), dtype=np.float32))
+        self.ck = bf16_round(g.standard_normal((1, self.S, self.Hk, self.D), dtype=np.float32))
+        inv = 10000.0 ** (-np.arange(0, self.D, 2, dtype=np.float32) / self.D)
+        ang = np.arange(self.S, dtype=np.float32)[:, None] * inv[None, :]
+        self.cc, self.cs = bf16_round(np.cos(ang)), bf16_round(np.sin(ang))
+        self.cpu_rows_total = self.S  # a "row" is one position of one sequence
+
+    def cpu_run(self, r0, r1):
+        from oracle import ops as O
+        return O.rope_qk_tables(self.cq[:, r0:r1], self.ck[:, r0:r1], self.cc[r0:r1],
+                                self.cs[r0:r1], "bf16", interleaved=self.interleaved)
+
+    def cpu_bytes_per_row(self):
+        return 2 * (self.H + self.Hk) * self.D * 2
+
+
+class RoPEInterleaved(RoPE):
+    name = "rope_qk_interleaved"
+    interleaved = True
+
+
+WORKLOADS = {"chain": Chain, "rmsnorm": RMSNorm, "swiglu": SwiGLU, "ce": CrossEntropy,
+             "rope": RoPE, "rope_interleaved": RoPEInterleaved}
+
+
+# ---------------------------------------------------------------------------
+# device timing
+def time_steps(fn, steps, stream, graph_steps=0):
+    """ms per step of fn() over `steps` steps, CUDA events on `stream`.  With
+    graph_steps > 0 the steps are captured into a CUDA graph of graph_steps
+    calls (host launch overhead removed) and the graph is replayed."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if graph_steps > 0:
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(graph_steps):
+                fn()
+        stream.wait_stream(side)
+        with torch.cuda.graph(g):
+            for _ in range(graph_steps):
+                fn()
+        reps = max(1, (steps + graph_steps - 1) // graph_steps)
+        g.replay()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / (reps * graph_steps), reps * graph_steps
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, steps
 
 
 # ---------------------------------------------------------------------------
@@ -421,6 +579,38 @@ def cpu_measure(wl, budget_s=10.0, threads=None, rows_per_task=64):
 
 
 # ---------------------------------------------------------------------------
+def measure_device(wl, args, stream, barrier, dist, device, local, sample_clocks=True):
+    """(ms per step max over ranks, ms this rank, steps timed, clock summary)."""
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ms, steps = time_steps(wl.step, args.steps, stream, wl.graph_steps if args.graph else 0)
+    barrier()
+    ms_max = ms
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    return ms_max, ms, steps, clk.summary()
+
+
+def measure_eager(wl, stream, steps=5):
+    if not hasattr(wl, "eager_step"):
+        return None
+    try:
+        for _ in range(2):
+            wl.eager_step()
+        torch.cuda.synchronize()
+        ms, _ = time_steps(wl.eager_step, steps, stream)
+        return ms
+    except torch.cuda.OutOfMemoryError:
+        torch.cuda.empty_cache()
+        return None
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -431,6 +621,11 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the device-only measurement of the other configurations")
+    ap.add_argument("--no-eager", action="store_true")
+    ap.add_argument("--graph", type=int, default=1,
+                    help="launch small workloads from a CUDA graph (1) or one by one (0)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -455,34 +650,23 @@ def main():
         if dist is not None:
             dist.barrier()
 
-    wl.setup(device, rank, world)
-    for _ in range(args.warmup):
-        wl.step()
-    torch.cuda.synchronize()
-
     stream = torch.cuda.current_stream(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        e0.record(stream)
-        for _ in range(args.steps):
-            wl.step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    ms_max = ms
-    if dist is not None:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    wl.setup(device, rank, world)
+    ms_max, ms, steps_timed, clocks = measure_device(wl, args, stream, barrier, dist, device, local)
 
     total_bytes = wl.bytes_per_step() * (world if wl.scaling == "weak" else 1)
     value = total_bytes / (ms_max * 1e-3) / 1e9
     peak, peak_kind = hbm_peak()
-    per_launch_ms = ms / wl.launches_per_step
-    achieved = wl.bytes_per_step() / wl.launches_per_step / (per_launch_ms * 1e-3) / 1e9
+    # the dominant kernel is timed with its step (any small companion
+    # kernels of the step count against it, which only lowers the figure)
+    achieved = wl.bytes_per_step() / (ms * 1e-3) / 1e9
+
+    eager = None
+    if not args.no_eager:
+        e_ms = measure_eager(wl, stream)
+        if e_ms is not None:
+            eager = {"ms_per_step": round(e_ms, 4), "speedup": round(e_ms / ms, 2),
+                     "what": "the reference's PyTorch expressions (ouroboros/specs.py), eager"}
 
     # end to end through the host-buffer API (pinned host in, pinned host out)
     e2e = None
@@ -501,12 +685,10 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e_ms = float(t.item())
         e_bytes = wl.e2e_bytes() if hasattr(wl, "e2e_bytes") else wl.bytes_per_step()
-        e_total = e_bytes * (world if wl.scaling == "weak" else 1)
-        if wl.scaling == "strong" and world > 1:
-            e_total = e_bytes * world
+        e_total = e_bytes * world
         e2e = {"value": round(e_total / (e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                "ms_per_step": round(e_ms, 4), "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "api": "b200k.host.run_rows_host (pinned host buffers)"}
+               "d2h_bytes_per_step": d2h, "api": wl.e2e_api()}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -524,24 +706,61 @@ def main():
         except Exception:
             traffic = None
 
+    # the other named configurations, device time only
+    extra = {}
+    launches = steps_timed * wl.launches_per_step
+    if not args.no_extra:
+        del wl
+        torch.cuda.empty_cache()
+        for name in ("rmsnorm", "swiglu", "rope", "rope_interleaved", "ce"):
+            if name == args.workload:
+                continue
+            w2 = WORKLOADS[name]()
+            w2.setup(device, rank, world)
+            a2 = argparse.Namespace(**vars(args))
+            a2.steps, a2.warmup = (40 if name != "ce" else 10), 5
+            m2, m2_local, st2, ck2 = measure_device(w2, a2, stream, barrier, dist, device, local)
+            launches += st2 * w2.launches_per_step
+            tb = w2.bytes_per_step() * (world if w2.scaling == "weak" else 1)
+            per_rank = w2.bytes_per_step() / (m2_local * 1e-3) / 1e9
+            entry = {"value": round(tb / (m2 * 1e-3) / 1e9, 2), "unit": "GB/s",
+                     "ms_per_step": round(m2, 5), "frac": round(per_rank / peak, 4),
+                     "scaling": w2.scaling, "config": w2.config(),
+                     "launch": "cuda_graph" if (args.graph and w2.graph_steps) else "stream"}
+            if not args.no_eager:
+                e2 = measure_eager(w2, stream, 3)
+                if e2 is not None:
+                    entry["eager_ms_per_step"] = round(e2, 4)
+                    entry["speedup_vs_eager"] = round(e2 / m2_local, 2)
+            extra[w2.name] = entry
+            del w2
+            torch.cuda.empty_cache()
+    else:
+        del wl
+
+    wl = WORKLOADS[args.workload]()
     line = {
         "metric": "achieved HBM GB/s (algorithmic bytes / step time), aggregate over GPUs",
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True,
         "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
-        "config": dict(wl.config(), parallelism=f"rows x{world}" if world > 1 else "1 GPU"),
+        "config": dict(wl.config(), parallelism=f"rows x{world}" if world > 1 else "1 GPU",
+                       launch="cuda_graph" if (args.graph and wl.graph_steps) else "stream"),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_source": peak_kind,
-                     "algorithmic_bytes_per_launch": wl.bytes_per_step() // wl.launches_per_step},
+                     "algorithmic_bytes_per_launch": wl.bytes_per_step()},
         "e2e": e2e,
         "cpu_baseline": cpu,
-        "gpu_launches": args.steps * wl.launches_per_step,
-        "clocks": clk.summary(),
+        "eager": eager,
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "other_configs": extra or None,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:
+        dist.barrier()
         dist.destroy_process_group()
 
 
