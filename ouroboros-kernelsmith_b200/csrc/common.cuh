@@ -236,19 +236,29 @@ struct Group {
 };
 
 template <typename Op>
-__device__ __forceinline__ float group_reduce(float v, const Group& g, float* red, Op op) {
+__device__ __forceinline__ float group_reduce(float v, const Group& g, float* red, Op op,
+                                             float identity) {
   const int width = g.G < 32 ? g.G : 32;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)
     if (o < width) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
   if (g.G > 32) {
-    const int nw = g.G >> 5;
-    if ((g.tx & 31) == 0) red[g.ty * 32 + (g.tx >> 5)] = v;
+    // warp partials -> the group's first warp combines them with shuffles
+    // (log depth) -> broadcast through shared memory
+    const int nw = g.G >> 5, w = g.tx >> 5, lane = g.tx & 31;
+    float* slot = red + g.ty * 32;
+    if (lane == 0) slot[w] = v;
     __syncthreads();
-    float t = red[g.ty * 32];
-    for (int i = 1; i < nw; ++i) t = op(t, red[g.ty * 32 + i]);
+    if (w == 0) {
+      float t = lane < nw ? slot[lane] : identity;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+        if (o < nw) t = op(t, __shfl_xor_sync(0xffffffffu, t, o));
+      if (lane == 0) slot[0] = t;
+    }
     __syncthreads();
-    v = t;
+    v = slot[0];
+    __syncthreads();
   }
   return v;
 }
@@ -257,10 +267,10 @@ struct OpSum { __device__ __forceinline__ float operator()(float a, float b) con
 struct OpMax { __device__ __forceinline__ float operator()(float a, float b) const { return fmaxf(a, b); } };
 
 __device__ __forceinline__ float group_sum(float v, const Group& g, float* red) {
-  return group_reduce(v, g, red, OpSum{});
+  return group_reduce(v, g, red, OpSum{}, 0.0f);
 }
 __device__ __forceinline__ float group_max(float v, const Group& g, float* red) {
-  return group_reduce(v, g, red, OpMax{});
+  return group_reduce(v, g, red, OpMax{}, -INFINITY);
 }
 
 // (max, sum-of-exp) pair merge for online logsumexp.  s is relative to m.
@@ -281,15 +291,27 @@ __device__ __forceinline__ void group_lse(float& m, float& s, const Group& g, fl
       lse_merge(m, s, m2, s2);
     }
   if (g.G > 32) {
-    const int nw = g.G >> 5;
-    float* rm = red;        // [R][32], R <= 16 when G > 32
-    float* rs = red + 512;  // [R][32]  (red must hold 1024 floats)
-    if ((g.tx & 31) == 0) { rm[g.ty * 32 + (g.tx >> 5)] = m; rs[g.ty * 32 + (g.tx >> 5)] = s; }
+    const int nw = g.G >> 5, w = g.tx >> 5, lane = g.tx & 31;
+    float* rm = red + g.ty * 32;        // [R <= 16][32]
+    float* rs = red + 512 + g.ty * 32;  // (red must hold 1024 floats)
+    if (lane == 0) { rm[w] = m; rs[w] = s; }
     __syncthreads();
-    float M = rm[g.ty * 32], S = rs[g.ty * 32];
-    for (int i = 1; i < nw; ++i) lse_merge(M, S, rm[g.ty * 32 + i], rs[g.ty * 32 + i]);
+    if (w == 0) {
+      float M = lane < nw ? rm[lane] : -INFINITY;
+      float S = lane < nw ? rs[lane] : 0.0f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+        if (o < nw) {
+          const float m2 = __shfl_xor_sync(0xffffffffu, M, o);
+          const float s2 = __shfl_xor_sync(0xffffffffu, S, o);
+          lse_merge(M, S, m2, s2);
+        }
+      if (lane == 0) { rm[0] = M; rs[0] = S; }
+    }
     __syncthreads();
-    m = M; s = S;
+    m = rm[0];
+    s = rs[0];
+    __syncthreads();
   }
 }
 

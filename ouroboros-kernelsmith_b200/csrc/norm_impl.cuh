@@ -115,16 +115,29 @@ __device__ __forceinline__ void group_moments(float& n, float& m, float& q, cons
       chan_merge(n, m, q, nb, mb, qb);
     }
   if (g.G > 32) {
-    const int nw = g.G >> 5;
-    float* rn = red;
-    float* rm = red + 512;
-    float* rq = red + 1024;
-    const int slot = g.ty * 32 + (g.tx >> 5);
-    if ((g.tx & 31) == 0) { rn[slot] = n; rm[slot] = m; rq[slot] = q; }
+    // warp partials -> the group's first warp merges them with shuffles
+    const int nw = g.G >> 5, w = g.tx >> 5, lane = g.tx & 31;
+    float* rn = red + g.ty * 32;
+    float* rm = red + 512 + g.ty * 32;
+    float* rq = red + 1024 + g.ty * 32;
+    if (lane == 0) { rn[w] = n; rm[w] = m; rq[w] = q; }
     __syncthreads();
-    n = rn[g.ty * 32]; m = rm[g.ty * 32]; q = rq[g.ty * 32];
-    for (int i = 1; i < nw; ++i)
-      chan_merge(n, m, q, rn[g.ty * 32 + i], rm[g.ty * 32 + i], rq[g.ty * 32 + i]);
+    if (w == 0) {
+      float a = lane < nw ? rn[lane] : 0.0f;
+      float b = lane < nw ? rm[lane] : 0.0f;
+      float c = lane < nw ? rq[lane] : 0.0f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+        if (o < nw) {
+          const float nb = __shfl_xor_sync(0xffffffffu, a, o);
+          const float mb = __shfl_xor_sync(0xffffffffu, b, o);
+          const float qb = __shfl_xor_sync(0xffffffffu, c, o);
+          chan_merge(a, b, c, nb, mb, qb);
+        }
+      if (lane == 0) { rn[0] = a; rm[0] = b; rq[0] = c; }
+    }
+    __syncthreads();
+    n = rn[0]; m = rm[0]; q = rq[0];
     __syncthreads();
   }
 }
@@ -441,22 +454,16 @@ static bool norm_try_tma(const NormArgs& a, cudaStream_t st, int* status) {
     G = G < 64 ? 64 : (G > kNormMaxThreads ? kNormMaxThreads : G);
   }
   const int64_t vneed = (nvec + G - 1) / G;
-  if (vneed > 8) return false;
-  const int V = vneed <= 4 ? 4 : 8;
+  if (vneed > 4) return false;  // longer rows: register / streaming kernels
   const int sms = sm_count();
+  auto kern = (vneed <= 2) ? norm_tma_kernel<T, 2, RESID, MODE, ACT> : norm_tma_kernel<T, 4, RESID, MODE, ACT>;
   PipeShape ps;
-  if (!choose_pipe_shape(stage, a.tma_cps, a.tma_stages, &ps)) return false;
+  if (!choose_pipe_shape(kern, G, stage, a.tma_cps, a.tma_stages, &ps)) return false;
   const int cps = ps.cps, S = ps.S;
   const size_t smem = RowPipe<RESID ? 2 : 1>::smem_bytes(S, a.N * (int64_t)sizeof(T));
   int64_t grid = (int64_t)sms * cps;
   if (grid > a.M) grid = a.M;
-
-  auto go = [&](auto kern) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<(unsigned)grid, G, smem, st>>>(a, S);
-  };
-  if (V == 4) go(norm_tma_kernel<T, 4, RESID, MODE, ACT>);
-  else go(norm_tma_kernel<T, 8, RESID, MODE, ACT>);
+  kern<<<(unsigned)grid, G, smem, st>>>(a, S);
   *status = check_launch("b2k_norm(tma)");
   return true;
 }

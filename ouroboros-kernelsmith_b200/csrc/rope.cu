@@ -4,10 +4,10 @@
 // b2k_rope (spec layout, per-row tables): one work item = one 16-byte vector
 // of x together with its partner (the vector D/2 away for the half-split
 // form, or the E/2 table entries of its pairs for the interleaved form).
-// b2k_rope_qk (attention layout): one block per (batch, position); its
-// threads cover every head of q and k for that position, so the position's
-// table row is read from HBM once and served from L1 for all heads; q and k
-// are rotated in the same launch.
+// b2k_rope_qk (attention layout): one block per 4 consecutive (batch,
+// position) pairs; its threads cover every head of q and k for those
+// positions, so a position's table row is read from HBM once and served from
+// L1 for all heads; q and k are rotated in the same launch.
 // b2k_norm_rope: RMSNorm over the head dim in registers, the normalised row
 // staged in shared memory so each element can read its rotation partner.
 #include "rowio.cuh"
@@ -128,53 +128,87 @@ struct RopeQkArgs {
   int D;
 };
 
+// block (per_head, heads_per_pass) over kRopePos consecutive positions:
+// threadIdx.x = vector slot within a head, threadIdx.y walks the heads; the
+// loads of all kRopePos positions are issued before any arithmetic so every
+// thread keeps kRopePos x 32 B of q/k in flight
+constexpr int kRopePos = 4;
+
 template <typename T, bool INTER>
-__global__ void __launch_bounds__(1024) rope_qk_kernel(const RopeQkArgs a, int per_head) {
+__global__ void __launch_bounds__(1024) rope_qk_kernel(const RopeQkArgs a) {
   constexpr int E = Traits<T>::E;
   constexpr int HP = E / 2;
-  const int64_t p = blockIdx.x;  // b * S + s
-  const int64_t s = p % a.S;
+  const int64_t npos = a.B * a.S;
+  const int64_t p0 = (int64_t)blockIdx.x * kRopePos;
   const int D = a.D, half = D / 2;
   const int heads = (int)(a.H + a.Hk);
-  const T* ct = static_cast<const T*>(a.cos) + s * half;
-  const T* st = static_cast<const T*>(a.sin) + s * half;
-  const int items = heads * per_head;
-  for (int it = threadIdx.x; it < items; it += blockDim.x) {
-    const int hh = it / per_head;
-    const int j = it - hh * per_head;
+  const int c = threadIdx.x * E;
+  for (int hh = threadIdx.y; hh < heads; hh += blockDim.y) {
     const bool isq = hh < a.H;
-    const int64_t base = isq ? (p * a.H + hh) * D : (p * a.Hk + (hh - a.H)) * D;
-    const T* src = (isq ? static_cast<const T*>(a.q) : static_cast<const T*>(a.k)) + base;
-    T* dst = (isq ? static_cast<T*>(a.qo) : static_cast<T*>(a.ko)) + base;
+    const int64_t hstride = isq ? a.H * D : a.Hk * D;  // elements per position
+    const int64_t hoff = (int64_t)(isq ? hh : hh - (int)a.H) * D;
+    const T* src = (isq ? static_cast<const T*>(a.q) : static_cast<const T*>(a.k)) + hoff;
+    T* dst = (isq ? static_cast<T*>(a.qo) : static_cast<T*>(a.ko)) + hoff;
     if (!INTER) {
-      const int c = j * E;  // first-half offset; partner at c + half
-      float x1[E], x2[E], cv[E], sv[E], o1[E], o2[E];
-      unpack<T>(ld_stream(src + c), x1);
-      unpack<T>(ld_stream(src + c + half), x2);
-      unpack<T>(ld_keep(ct + c), cv);
-      unpack<T>(ld_keep(st + c), sv);
+      uint4 r1[kRopePos], r2[kRopePos], rc[kRopePos], rs[kRopePos];
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        o1[e] = x1[e] * cv[e] - x2[e] * sv[e];
-        o2[e] = x2[e] * cv[e] + x1[e] * sv[e];
+      for (int u = 0; u < kRopePos; ++u) {
+        const int64_t p = p0 + u;
+        if (p < npos) {
+          const int64_t s = p % a.S;
+          r1[u] = ld_stream(src + p * hstride + c);
+          r2[u] = ld_stream(src + p * hstride + c + half);
+          rc[u] = ld_keep(static_cast<const T*>(a.cos) + s * half + c);
+          rs[u] = ld_keep(static_cast<const T*>(a.sin) + s * half + c);
+        }
       }
-      st_stream(dst + c, pack<T>(o1));
-      st_stream(dst + c + half, pack<T>(o2));
+#pragma unroll
+      for (int u = 0; u < kRopePos; ++u) {
+        const int64_t p = p0 + u;
+        if (p < npos) {
+          float x1[E], x2[E], cv[E], sv[E], o1[E], o2[E];
+          unpack<T>(r1[u], x1);
+          unpack<T>(r2[u], x2);
+          unpack<T>(rc[u], cv);
+          unpack<T>(rs[u], sv);
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            o1[e] = x1[e] * cv[e] - x2[e] * sv[e];
+            o2[e] = x2[e] * cv[e] + x1[e] * sv[e];
+          }
+          st_stream(dst + p * hstride + c, pack<T>(o1));
+          st_stream(dst + p * hstride + c + half, pack<T>(o2));
+        }
+      }
     } else {
-      const int c = j * E;  // E elements = E/2 pairs; table entries c/2..
-      float xv[E], o[E];
-      unpack<T>(ld_stream(src + c), xv);
-      const uint2 cw = __ldg(reinterpret_cast<const uint2*>(ct + c / 2));
-      const uint2 sw = __ldg(reinterpret_cast<const uint2*>(st + c / 2));
-      float tmp[E];
-      unpack<T>(make_uint4(cw.x, cw.y, sw.x, sw.y), tmp);
+      uint4 rx[kRopePos];
+      uint2 rc[kRopePos], rs[kRopePos];
 #pragma unroll
-      for (int i = 0; i < HP; ++i) {
-        const float cc = tmp[i], ss = tmp[HP + i];
-        o[2 * i] = xv[2 * i] * cc - xv[2 * i + 1] * ss;
-        o[2 * i + 1] = xv[2 * i + 1] * cc + xv[2 * i] * ss;
+      for (int u = 0; u < kRopePos; ++u) {
+        const int64_t p = p0 + u;
+        if (p < npos) {
+          const int64_t s = p % a.S;
+          rx[u] = ld_stream(src + p * hstride + c);
+          rc[u] = __ldg(reinterpret_cast<const uint2*>(static_cast<const T*>(a.cos) + s * half + c / 2));
+          rs[u] = __ldg(reinterpret_cast<const uint2*>(static_cast<const T*>(a.sin) + s * half + c / 2));
+        }
       }
-      st_stream(dst + c, pack<T>(o));
+#pragma unroll
+      for (int u = 0; u < kRopePos; ++u) {
+        const int64_t p = p0 + u;
+        if (p < npos) {
+          float xv[E], cs[E], o[E];
+          unpack<T>(rx[u], xv);
+          unpack<T>(make_uint4(rc[u].x, rc[u].y, rs[u].x, rs[u].y), cs);
+#pragma unroll
+          for (int i = 0; i < HP; ++i) {
+            const float cc = cs[i], ss = cs[HP + i];
+            o[2 * i] = xv[2 * i] * cc - xv[2 * i + 1] * ss;
+            o[2 * i + 1] = xv[2 * i + 1] * cc + xv[2 * i] * ss;
+          }
+          st_stream(dst + p * hstride + c, pack<T>(o));
+        }
+      }
     }
   }
 }
@@ -371,15 +405,17 @@ extern "C" int b2k_rope_qk(const void* q, const void* k, const void* cos, const 
       per_head = (int)(D / E);
     }
     if (vec) {
-      const int64_t items = (H + Hk) * per_head;
-      int threads = (int)((items + 31) / 32 * 32);
-      threads = threads > 1024 ? 1024 : threads;
-      const int64_t grid = B * S;
+      B2K_REQUIRE(per_head <= 1024, "b2k_rope_qk: head dim too large");
+      int hpp = 1024 / per_head;
+      const int64_t heads = H + Hk;
+      if (hpp > heads) hpp = (int)heads;
+      const dim3 block(per_head, hpp);
+      const int64_t grid = (B * S + kRopePos - 1) / kRopePos;
       B2K_REQUIRE(grid <= 0x7fffffffLL, "b2k_rope_qk: too many positions");
       if (interleaved)
-        rope_qk_kernel<T, true><<<(unsigned)grid, threads, 0, st>>>(a, per_head);
+        rope_qk_kernel<T, true><<<(unsigned)grid, block, 0, st>>>(a);
       else
-        rope_qk_kernel<T, false><<<(unsigned)grid, threads, 0, st>>>(a, per_head);
+        rope_qk_kernel<T, false><<<(unsigned)grid, block, 0, st>>>(a);
     } else {
       const int64_t items = B * S * (H + Hk) * (D / 2);
       if (interleaved)

@@ -13,6 +13,8 @@
 // copied as one bulk transfer of N * sizeof(T) bytes (16-byte multiple).
 #pragma once
 
+#include <mutex>
+
 #include "tma.cuh"
 
 namespace b2k {
@@ -105,22 +107,103 @@ struct RowPipe {
 };
 
 // Host: pipeline shape for rows of `stage_bytes` (all inputs of one row).
-// Returns false when the rows do not fit (the caller uses another kernel).
+// More resident blocks per SM hide the per-row reduction latency better than
+// a deeper ring, so the shape takes as many blocks as registers, threads and
+// shared memory allow (up to 8) and then as many stages (2..4) as fit the
+// shared-memory budget.  Explicit want_cps / want_stages override.  Returns
+// false when the rows do not fit (the caller uses another kernel).
 struct PipeShape {
   int cps, S;
 };
 
-inline bool choose_pipe_shape(int64_t stage_bytes, int want_cps, int want_stages,
-                              PipeShape* ps) {
+// Raises the kernel's dynamic shared-memory cap once (to the whole per-block
+// maximum); the launch itself asks for what it needs.
+template <typename Kernel>
+inline void allow_max_dynamic_smem(Kernel kern) {
+  static std::mutex mu;
+  static const void* done[256];
+  static int ndone = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < ndone; ++i)
+    if (done[i] == (const void*)kern) return;
+  int dev = 0, optin = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  cudaFuncAttributes fa;
+  cudaFuncGetAttributes(&fa, kern);
+  const int cap = optin - (int)fa.sharedSizeBytes;
+  if (cap > 0) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+  cudaGetLastError();
+  if (ndone < 256) done[ndone++] = (const void*)kern;
+}
+
+template <typename Kernel>
+inline bool choose_pipe_shape_uncached(Kernel kern, int threads, int64_t stage_bytes,
+                                       int want_cps, int want_stages, PipeShape* ps) {
   const int64_t budget = 200 << 10;  // dynamic shared memory per SM
-  int cps = want_cps > 0 ? want_cps : 2;
-  int S = want_stages > 0 ? want_stages : 4;
-  while (S > 2 && (int64_t)cps * S * stage_bytes > budget) --S;
-  while (cps > 1 && (int64_t)cps * S * stage_bytes > budget) --cps;
-  if ((int64_t)cps * S * stage_bytes > budget) return false;
-  ps->cps = cps;
-  ps->S = S;
-  return true;
+  if (want_cps > 0 || want_stages > 0) {
+    int cps = want_cps > 0 ? want_cps : 2;
+    int S = want_stages > 0 ? want_stages : 4;
+    while (S > 2 && (int64_t)cps * S * stage_bytes > budget) --S;
+    while (cps > 1 && (int64_t)cps * S * stage_bytes > budget) --cps;
+    if ((int64_t)cps * S * stage_bytes > budget) return false;
+    ps->cps = cps;
+    ps->S = S;
+    return true;
+  }
+  for (int cps = 8; cps >= 1; --cps) {
+    int S = 4;
+    while (S > 2 && (int64_t)cps * S * stage_bytes > budget) --S;
+    if ((int64_t)cps * S * stage_bytes > budget) continue;
+    const size_t smem = (size_t)S * (size_t)stage_bytes + (size_t)S * sizeof(uint64_t);
+    int resident = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, threads, smem) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      continue;
+    }
+    if (resident >= cps) {
+      ps->cps = cps;
+      ps->S = S;
+      return true;
+    }
+  }
+  return false;
+}
+
+// Cached per (kernel, threads, stage bytes, overrides): the occupancy query
+// runs once, later launches pay a table lookup.
+template <typename Kernel>
+inline bool choose_pipe_shape(Kernel kern, int threads, int64_t stage_bytes, int want_cps,
+                              int want_stages, PipeShape* ps) {
+  struct Entry {
+    const void* k;
+    int threads, cps, stages;
+    int64_t stage;
+    PipeShape ps;
+    bool ok;
+  };
+  static std::mutex mu;
+  static Entry cache[512];
+  static int n = 0;
+  allow_max_dynamic_smem(kern);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < n; ++i) {
+      const Entry& e = cache[i];
+      if (e.k == (const void*)kern && e.threads == threads && e.stage == stage_bytes &&
+          e.cps == want_cps && e.stages == want_stages) {
+        *ps = e.ps;
+        return e.ok;
+      }
+    }
+  }
+  PipeShape r{1, 2};
+  const bool ok = choose_pipe_shape_uncached(kern, threads, stage_bytes, want_cps, want_stages, &r);
+  std::lock_guard<std::mutex> lock(mu);
+  if (n < 512) cache[n++] = Entry{(const void*)kern, threads, want_cps, want_stages, stage_bytes, r, ok};
+  *ps = r;
+  return ok;
 }
 
 }  // namespace b2k

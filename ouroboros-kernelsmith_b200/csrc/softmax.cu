@@ -274,22 +274,22 @@ static int softmax_launch(const SoftmaxArgs& a, cudaStream_t st) {
   const int64_t nvec = (a.N + E - 1) / E;
   const int64_t row_bytes = (int64_t)a.N * sizeof(T);
   if (use_tma && a.aligned && nvec >= 256 && row_bytes <= (64 << 10)) {
-    int G = next_pow2((nvec + 3) / 4);
+    static const int want_g = env_int("B2K_TMA_THREADS", 0);
+    int G = want_g > 0 ? want_g : next_pow2((nvec + 3) / 4);
     G = G < 64 ? 64 : (G > kSmMaxThreads ? kSmMaxThreads : G);
     const int64_t vneed = (nvec + G - 1) / G;
     PipeShape ps;
-    if (vneed <= 8 && choose_pipe_shape(row_bytes, env_int("B2K_TMA_CPS", 0),
-                                        env_int("B2K_TMA_STAGES", 0), &ps)) {
-      const size_t smem = RowPipe<1>::smem_bytes(ps.S, row_bytes);
-      int64_t grid = (int64_t)sm_count() * ps.cps;
-      if (grid > a.M) grid = a.M;
-      auto go = [&](auto kern) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (vneed <= 4) {
+      auto kern = vneed <= 2 ? softmax_tma_kernel<T, KIND, 2> : softmax_tma_kernel<T, KIND, 4>;
+      static const int want_cps = env_int("B2K_TMA_CPS", 0);
+      static const int want_st = env_int("B2K_TMA_STAGES", 0);
+      if (choose_pipe_shape(kern, G, row_bytes, want_cps, want_st, &ps)) {
+        const size_t smem = RowPipe<1>::smem_bytes(ps.S, row_bytes);
+        int64_t grid = (int64_t)sm_count() * ps.cps;
+        if (grid > a.M) grid = a.M;
         kern<<<(unsigned)grid, G, smem, st>>>(a, ps.S);
-      };
-      if (vneed <= 4) go(softmax_tma_kernel<T, KIND, 4>);
-      else go(softmax_tma_kernel<T, KIND, 8>);
-      return check_launch("b2k_softmax(tma)");
+        return check_launch("b2k_softmax(tma)");
+      }
     }
   }
   RowCfg cfg;
