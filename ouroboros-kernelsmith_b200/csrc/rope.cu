@@ -129,10 +129,12 @@ struct RopeQkArgs {
 };
 
 // block (per_head, heads_per_pass) over kRopePos consecutive positions:
-// threadIdx.x = vector slot within a head, threadIdx.y walks the heads; the
-// loads of all kRopePos positions are issued before any arithmetic so every
-// thread keeps kRopePos x 32 B of q/k in flight
-constexpr int kRopePos = 4;
+// threadIdx.x = vector slot within a head, threadIdx.y walks the heads.
+// Every thread moves two 16-byte vectors of a head: the half-split form pairs
+// element i with i + D/2, the interleaved form takes vectors c and c + D/2
+// (both whole pairs) so each thread keeps 32 B of q/k in flight.  (Measured
+// on B200: one position per block beats 2 or 4 per block.)
+constexpr int kRopePos = 1;
 
 template <typename T, bool INTER>
 __global__ void __launch_bounds__(1024) rope_qk_kernel(const RopeQkArgs a) {
@@ -181,32 +183,39 @@ __global__ void __launch_bounds__(1024) rope_qk_kernel(const RopeQkArgs a) {
         }
       }
     } else {
-      uint4 rx[kRopePos];
-      uint2 rc[kRopePos], rs[kRopePos];
+      uint4 rx[kRopePos][2];
+      uint2 rc[kRopePos][2], rs[kRopePos][2];
 #pragma unroll
       for (int u = 0; u < kRopePos; ++u) {
         const int64_t p = p0 + u;
         if (p < npos) {
           const int64_t s = p % a.S;
-          rx[u] = ld_stream(src + p * hstride + c);
-          rc[u] = __ldg(reinterpret_cast<const uint2*>(static_cast<const T*>(a.cos) + s * half + c / 2));
-          rs[u] = __ldg(reinterpret_cast<const uint2*>(static_cast<const T*>(a.sin) + s * half + c / 2));
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int cc = c + h2 * half;
+            rx[u][h2] = ld_stream(src + p * hstride + cc);
+            rc[u][h2] = __ldg(reinterpret_cast<const uint2*>(static_cast<const T*>(a.cos) + s * half + cc / 2));
+            rs[u][h2] = __ldg(reinterpret_cast<const uint2*>(static_cast<const T*>(a.sin) + s * half + cc / 2));
+          }
         }
       }
 #pragma unroll
       for (int u = 0; u < kRopePos; ++u) {
         const int64_t p = p0 + u;
         if (p < npos) {
-          float xv[E], cs[E], o[E];
-          unpack<T>(rx[u], xv);
-          unpack<T>(make_uint4(rc[u].x, rc[u].y, rs[u].x, rs[u].y), cs);
 #pragma unroll
-          for (int i = 0; i < HP; ++i) {
-            const float cc = cs[i], ss = cs[HP + i];
-            o[2 * i] = xv[2 * i] * cc - xv[2 * i + 1] * ss;
-            o[2 * i + 1] = xv[2 * i + 1] * cc + xv[2 * i] * ss;
+          for (int h2 = 0; h2 < 2; ++h2) {
+            float xv[E], cs[E], o[E];
+            unpack<T>(rx[u][h2], xv);
+            unpack<T>(make_uint4(rc[u][h2].x, rc[u][h2].y, rs[u][h2].x, rs[u][h2].y), cs);
+#pragma unroll
+            for (int i = 0; i < HP; ++i) {
+              const float cc = cs[i], ss = cs[HP + i];
+              o[2 * i] = xv[2 * i] * cc - xv[2 * i + 1] * ss;
+              o[2 * i + 1] = xv[2 * i + 1] * cc + xv[2 * i] * ss;
+            }
+            st_stream(dst + p * hstride + c + h2 * half, pack<T>(o));
           }
-          st_stream(dst + p * hstride + c, pack<T>(o));
         }
       }
     }
@@ -400,9 +409,9 @@ extern "C" int b2k_rope_qk(const void* q, const void* k, const void* cos, const 
             ((D / 2) * es) % 16 == 0;
       per_head = (int)(D / 2 / E);
     } else {
-      vec = base16 && D % E == 0 && ((uintptr_t)cos % 8 == 0) && ((uintptr_t)sin % 8 == 0) &&
-            ((D / 2) * es) % 8 == 0;
-      per_head = (int)(D / E);
+      vec = base16 && (D / 2) % E == 0 && ((uintptr_t)cos % 8 == 0) &&
+            ((uintptr_t)sin % 8 == 0) && ((D / 2) * es) % 8 == 0;
+      per_head = (int)(D / 2 / E);
     }
     if (vec) {
       B2K_REQUIRE(per_head <= 1024, "b2k_rope_qk: head dim too large");
