@@ -130,6 +130,11 @@ class Workload:
     def e2e_api(self):
         return "b200k.host.run_rows_host (pinned host buffers, copies overlapped with kernels)"
 
+    ROWS_ATTR = "M"
+
+    def set_rows(self, n):
+        setattr(self, self.ROWS_ATTR, int(n))
+
     def setup(self, device, rank, world): ...
     def step(self): ...
     def bytes_per_step(self) -> int: ...
@@ -336,6 +341,7 @@ class CrossEntropy(Workload):
     scaling = "strong"
     launches_per_step = 3  # row losses, shard reduce, mean
     T, V = 32768, 128256
+    ROWS_ATTR = "T"
 
     def setup(self, device, rank, world):
         import b200k
@@ -427,6 +433,7 @@ class RoPE(Workload):
     name = "rope_qk"
     B, S, H, Hk, D = 8, 4096, 32, 8, 128
     interleaved = False
+    ROWS_ATTR = "B"
 
     def setup(self, device, rank, world):
         import b200k
@@ -626,6 +633,9 @@ def main():
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--graph", type=int, default=1,
                     help="launch small workloads from a CUDA graph (1) or one by one (0)")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override the row count of the workload (M; batch for rope; "
+                         "tokens for ce) — small cases for profiler captures")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -633,6 +643,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     wl = WORKLOADS[args.workload]()
+    if args.rows > 0:
+        wl.set_rows(args.rows)
 
     if args.impl == "reference":
         return run_reference(args, wl, rank, world)
@@ -699,12 +711,16 @@ def main():
 
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
+    if os.path.exists(tp) and args.rows == 0 and world == 1:
         try:
             with open(tp) as f:
                 traffic = json.load(f).get(wl.name)
         except Exception:
             traffic = None
+
+    # the fields of the line that need the configured workload
+    wl_cfg, wl_bytes = wl.config(), wl.bytes_per_step()
+    wl_scaling, wl_dtype, wl_graph = wl.scaling, wl.dtype, wl.graph_steps
 
     # the other named configurations, device time only
     extra = {}
@@ -716,7 +732,7 @@ def main():
             if name == args.workload:
                 continue
             w2 = WORKLOADS[name]()
-            w2.setup(device, rank, world)
+            w2.setup(device, rank, world)  # full configuration (no --rows)
             a2 = argparse.Namespace(**vars(args))
             a2.steps, a2.warmup = (40 if name != "ce" else 10), 5
             m2, m2_local, st2, ck2 = measure_device(w2, a2, stream, barrier, dist, device, local)
@@ -738,18 +754,17 @@ def main():
     else:
         del wl
 
-    wl = WORKLOADS[args.workload]()
     line = {
         "metric": "achieved HBM GB/s (algorithmic bytes / step time), aggregate over GPUs",
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True,
-        "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
-        "config": dict(wl.config(), parallelism=f"rows x{world}" if world > 1 else "1 GPU",
-                       launch="cuda_graph" if (args.graph and wl.graph_steps) else "stream"),
+        "scaling": wl_scaling, "vs_baseline": None, "dtype": wl_dtype, "data": "synthetic",
+        "config": dict(wl_cfg, parallelism=f"rows x{world}" if world > 1 else "1 GPU",
+                       launch="cuda_graph" if (args.graph and wl_graph) else "stream"),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_source": peak_kind,
-                     "algorithmic_bytes_per_launch": wl.bytes_per_step()},
+                     "algorithmic_bytes_per_launch": wl_bytes},
         "e2e": e2e,
         "cpu_baseline": cpu,
         "eager": eager,
