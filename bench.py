@@ -666,7 +666,10 @@ def main():
     wl.setup(device, rank, world)
     ms_max, ms, steps_timed, clocks = measure_device(wl, args, stream, barrier, dist, device, local)
 
-    total_bytes = wl.bytes_per_step() * (world if wl.scaling == "weak" else 1)
+    # every rank's bytes_per_step is its own share (a full configuration for
+    # the weakly scaled workloads, its row shard for ce), so the job moves
+    # world x that per step
+    total_bytes = wl.bytes_per_step() * world
     value = total_bytes / (ms_max * 1e-3) / 1e9
     peak, peak_kind = hbm_peak()
     # the dominant kernel is timed with its step (any small companion
@@ -737,7 +740,7 @@ def main():
             a2.steps, a2.warmup = (40 if name != "ce" else 10), 5
             m2, m2_local, st2, ck2 = measure_device(w2, a2, stream, barrier, dist, device, local)
             launches += st2 * w2.launches_per_step
-            tb = w2.bytes_per_step() * (world if w2.scaling == "weak" else 1)
+            tb = w2.bytes_per_step() * world
             per_rank = w2.bytes_per_step() / (m2_local * 1e-3) / 1e9
             entry = {"value": round(tb / (m2 * 1e-3) / 1e9, 2), "unit": "GB/s",
                      "ms_per_step": round(m2, 5), "frac": round(per_rank / peak, 4),
