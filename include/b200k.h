@@ -90,6 +90,12 @@ const char* b2k_last_error(void);
  * kernels have no device-side waits). */
 unsigned b2k_pipeline_timeouts(int reset);
 
+/* Exercises the bounded device wait of the pipelines: one block waits on a
+ * barrier that nothing completes, gives up after limit_ns (<= 10 s), adds one
+ * to the timeout counter and writes *status = 1 (device int) — the context
+ * stays usable.  No reference counterpart (failure-path self-test). */
+int b2k_selftest_bounded_wait(unsigned long long limit_ns, int* status, void* stream);
+
 /* Residual -> {RMSNorm, L2, LayerNorm} -> affine -> epilogue, one row per
  * thread group, row held in registers (rows longer than the register budget
  * stream through L2 in two or three passes).

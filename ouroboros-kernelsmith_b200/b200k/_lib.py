@@ -31,6 +31,7 @@ SIGNATURES = {
     "b2k_version": (c_int, []),
     "b2k_last_error": (ctypes.c_char_p, []),
     "b2k_pipeline_timeouts": (ctypes.c_uint, [c_int]),
+    "b2k_selftest_bounded_wait": (c_int, [ctypes.c_ulonglong, c_void_p, c_void_p]),
     "b2k_norm": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                          c_int64, c_void_p, c_int64, c_int64, c_int64, c_int, c_int, c_int, c_int,
                          c_float, c_void_p]),

@@ -23,6 +23,8 @@
 #pragma once
 
 #include "rowio.cuh"
+#include <cooperative_groups.h>
+
 #include "rowpipe.cuh"
 
 namespace b2k {
@@ -439,6 +441,170 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
 }
 
 // ---------------------------------------------------------------------------
+// Few long rows (rmsnorm_wide, specs.py:866-871: M <= 32, N up to 131072):
+// a thread-block cluster of C CTAs splits each row into C contiguous
+// segments held in registers; every CTA reduces its segment, the partials are
+// exchanged through distributed shared memory, and each CTA normalises its
+// own segment.  One read and one write per element, M*C CTAs in flight
+// instead of M.
+template <typename T, bool RESID, int MODE>
+__global__ void __launch_bounds__(kNormMaxThreads) norm_cluster_kernel(const NormArgs a,
+                                                                       const int seg) {
+  namespace cg = cooperative_groups;
+  constexpr int E = Traits<T>::E;
+  constexpr int H = E / 2;
+  constexpr int V = 4;
+  constexpr bool HAS_W = MODE != NM_L2;
+  __shared__ float red[1536];
+  __shared__ float part[3];
+  __shared__ float fin[2];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int C = (int)cluster.num_blocks();
+  const Group g;
+  const int64_t row = blockIdx.y;
+  const int N = (int)a.N;
+  const int c0 = rank * seg;
+  const int nh = N - c0 < seg ? (N - c0 > 0 ? N - c0 : 0) : seg;  // elements of this segment
+  const T* xr = static_cast<const T*>(a.x) + row * a.ldx + c0;
+  const T* rr = RESID ? static_cast<const T*>(a.r) + row * a.ldr + c0 : nullptr;
+
+  float2 hv[V][H];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * g.G + g.tx) * E;
+    load_pairs<T, true>(hv[v], xr, c, nh, true);
+    if (RESID) {
+      float2 t[H];
+      load_pairs<T, true>(t, rr, c, nh, true);
+#pragma unroll
+      for (int j = 0; j < H; ++j) hv[v][j] = add2(hv[v][j], t[j]);
+    }
+  }
+  if (a.h != nullptr) {
+    T* hrow = static_cast<T*>(a.h) + row * a.ldh + c0;
+#pragma unroll
+    for (int v = 0; v < V; ++v) store_pairs<T>(hrow, (v * g.G + g.tx) * E, nh, true, hv[v]);
+  }
+  // partial statistics of the segment
+  if constexpr (MODE == NM_LN) {
+    float2 s2 = f2s(0.0f);
+    float cnt = 0.0f;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * g.G + g.tx) * E;
+      if (c < nh) {
+#pragma unroll
+        for (int j = 0; j < H; ++j) s2 = add2(s2, hv[v][j]);
+        cnt += (float)E;
+      }
+    }
+    float m = cnt > 0.0f ? (s2.x + s2.y) / cnt : 0.0f, q = 0.0f;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * g.G + g.tx) * E;
+      if (c < nh) {
+#pragma unroll
+        for (int j = 0; j < H; ++j) {
+          const float2 d = add2(hv[v][j], f2s(-m));
+          q = fmaf(d.x, d.x, fmaf(d.y, d.y, q));
+        }
+      }
+    }
+    group_moments(cnt, m, q, g, red);
+    if (g.tx == 0) { part[0] = cnt; part[1] = m; part[2] = q; }
+  } else {
+    float2 q2 = f2s(0.0f);
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+#pragma unroll
+      for (int j = 0; j < H; ++j) q2 = fma2(hv[v][j], hv[v][j], q2);
+    const float s = group_sum(q2.x + q2.y, g, red);
+    if (g.tx == 0) part[0] = s;
+  }
+  cluster.sync();  // partials of every segment visible cluster-wide
+  if (g.tx == 0) {
+    float mu = 0.0f, rs;
+    if constexpr (MODE == NM_LN) {
+      float n = 0.0f, m = 0.0f, q = 0.0f;
+      for (int r = 0; r < C; ++r) {
+        const float* pr = cluster.map_shared_rank(part, r);
+        chan_merge(n, m, q, pr[0], pr[1], pr[2]);
+      }
+      mu = m;
+      rs = rsqrtf(q / (float)N + a.eps);
+    } else {
+      float s = 0.0f;
+      for (int r = 0; r < C; ++r) s += *cluster.map_shared_rank(part, r);
+      rs = rsqrtf((MODE == NM_L2 ? s : s / (float)N) + a.eps);
+    }
+    fin[0] = mu;
+    fin[1] = rs;
+  }
+  __syncthreads();
+  const float2 nmu2 = f2s(-fin[0]), rs2 = f2s(fin[1]);
+  T* yrow = static_cast<T*>(a.y) + row * a.ldy + c0;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * g.G + g.tx) * E;
+    if (c < nh) {
+      float2 wv[H], bv[H], out[H];
+      if constexpr (HAS_W) load_pairs<T, false>(wv, static_cast<const T*>(a.w) + c0, c, nh, true);
+      if constexpr (MODE == NM_LN) load_pairs<T, false>(bv, static_cast<const T*>(a.b) + c0, c, nh, true);
+#pragma unroll
+      for (int j = 0; j < H; ++j)
+        out[j] = norm_pair<T, MODE, 0>(hv[v][j], nmu2, rs2, HAS_W ? wv[j] : f2s(1.0f),
+                                       MODE == NM_LN ? bv[j] : f2s(0.0f));
+      store_pairs<T>(yrow, c, nh, true, out);
+    }
+  }
+  cluster.sync();  // no block leaves while another may still read its partial
+}
+
+template <typename T, bool RESID, int MODE>
+static bool norm_try_cluster(const NormArgs& a, cudaStream_t st, int* status) {
+  constexpr int E = Traits<T>::E;
+  if (!a.aligned || a.M > 64 || a.N / E < 2048) return false;
+  const int sms = sm_count();
+  // cluster size: enough blocks to cover the SMs about twice, within 2..16,
+  // and large enough that a segment fits 512 threads x 4 vectors
+  int C = next_pow2((2 * sms + a.M - 1) / a.M);
+  C = C < 2 ? 2 : (C > 16 ? 16 : C);
+  int64_t seg = 0;
+  for (;; C <<= 1) {
+    if (C > 16) return false;
+    seg = ((a.N + C - 1) / C + E - 1) / E * E;
+    if (seg / E <= (int64_t)kNormMaxThreads * 4) break;
+  }
+  int G = next_pow2((seg / E + 3) / 4);
+  G = G < 64 ? 64 : (G > kNormMaxThreads ? kNormMaxThreads : G);
+  auto kern = norm_cluster_kernel<T, RESID, MODE>;
+  if (C > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+                   cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)C, (unsigned)a.M, 1);
+  cfg.blockDim = dim3((unsigned)G, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a, (int)seg) != cudaSuccess) {
+    cudaGetLastError();  // cluster shape not available: use another kernel
+    return false;
+  }
+  *status = check_launch("b2k_norm(cluster)");
+  return true;
+}
+
+// ---------------------------------------------------------------------------
 // launch
 template <typename T, bool RESID, int MODE, int ACT>
 static bool norm_try_tma(const NormArgs& a, cudaStream_t st, int* status) {
@@ -473,6 +639,9 @@ static int norm_launch_resid(const NormArgs& a, cudaStream_t st) {
   constexpr int E = Traits<T>::E;
   int status;
   if (norm_try_tma<T, RESID, MODE, ACT>(a, st, &status)) return status;
+  if constexpr (ACT == 0) {
+    if (a.use_tma && norm_try_cluster<T, RESID, MODE>(a, st, &status)) return status;
+  }
   RowCfg cfg;
   if (choose_row_cfg(a.N, E, a.g_target, &cfg, 4, kNormMaxThreads)) {
     const dim3 block(cfg.G, cfg.R);

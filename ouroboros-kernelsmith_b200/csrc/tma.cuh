@@ -77,14 +77,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Bounded wait for the phase with `parity` to complete.  Returns false on
-// timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait for the phase with `parity` to complete.  Returns false
+// after `limit_ns` of global time without completion.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer() - t0 > kTimeoutNs) return false;
+    if ((i & 255u) == 0 && globaltimer() - t0 > limit_ns) return false;
   }
 }
 
