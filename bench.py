@@ -523,6 +523,206 @@ WORKLOADS = {"chain": Chain, "rmsnorm": RMSNorm, "swiglu": SwiGLU, "ce": CrossEn
 
 
 # ---------------------------------------------------------------------------
+# E2E MLP block (ouroboros/e2e_block_bench.py:94-148): add_rmsnorm -> gate/up
+# GEMMs -> swiglu -> down GEMM, fp16, GEMMs by cuBLAS (torch.matmul) in every
+# path; the b200k path replaces the two non-GEMM ops.
+def run_mlp_block(args, device):
+    import b200k
+    R = args.rows or 8192
+    H, F = 4096, 11008
+    g = torch.Generator(device=device).manual_seed(7)
+    rnd = lambda *shape, scale=1.0: (torch.randn(shape, generator=g, device=device) * scale).half()
+    x, res, w = rnd(R, H), rnd(R, H), rnd(H)
+    Wg, Wu, Wd = rnd(H, F, scale=H ** -0.5), rnd(H, F, scale=H ** -0.5), rnd(F, H, scale=F ** -0.5)
+
+    def block_eager(x, res, w, Wg, Wu, Wd):
+        h = x.float() + res.float()
+        rms = torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-6)
+        hn = (h * rms).to(x.dtype) * w
+        gate, up = hn @ Wg, hn @ Wu
+        return (torch.nn.functional.silu(gate) * up) @ Wd
+
+    def block_ours(x, res, w, Wg, Wu, Wd):
+        hn = b200k.add_rmsnorm(x, res, w)
+        gate, up = hn @ Wg, hn @ Wu
+        return b200k.swiglu(gate, up) @ Wd
+
+    def nongemm_eager(x, res, w):
+        h = x.float() + res.float()
+        rms = torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-6)
+        return (h * rms).to(x.dtype) * w
+
+    inputs = (x, res, w, Wg, Wu, Wd)
+    ref = block_eager(*inputs)
+    out = block_ours(*inputs)
+    err = float((out.float() - ref.float()).abs().max())
+    ok = bool(torch.allclose(out.float(), ref.float(), rtol=3e-2, atol=2e-2))
+    stream = torch.cuda.current_stream(device)
+
+    def t(fn, *a):
+        for _ in range(3):
+            fn(*a)
+        torch.cuda.synchronize()
+        return time_steps(lambda: fn(*a), max(10, args.steps), stream)[0]
+
+    te, to = t(block_eager, *inputs), t(block_ours, *inputs)
+    tne, tno = t(nongemm_eager, x, res, w), t(b200k.add_rmsnorm, x, res, w)
+    line = {"metric": "MLP block tokens/s (add_rmsnorm -> GEMMs -> swiglu -> GEMM)",
+            "value": round(R / (to * 1e-3), 1), "unit": "tokens/s", "n_gpus": 1,
+            "higher_is_better": True, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "mlp_block", "rows": R, "hidden": H, "ffn": F},
+            "correct_vs_eager": ok, "max_abs_err_vs_eager": err,
+            "block_ms": {"eager": round(te, 4), "b200k": round(to, 4)},
+            "speedup_vs_eager": round(te / to, 4),
+            "nongemm_ms": {"eager": round(tne, 4), "b200k": round(tno, 4)},
+            "amdahl_bound_vs_eager": round(1.0 / (1.0 - (tne - tno) / te), 4)}
+    print(json.dumps(line), flush=True)
+    return 0 if ok else 1
+
+
+# ---------------------------------------------------------------------------
+# Shape grid (ouroboros/rebench_shapes.py:37-41): every listed op at every
+# (M, N) cell in fp16 and bf16 — b200k GB/s and % of the HBM peak, torch eager
+# time of the reference expression, and a parity check of sampled rows
+# against the CPU oracle.  One JSON line per op.
+MATRIX_GRID = [(1024, 4096), (4096, 4096), (8192, 4096), (4096, 8192), (16384, 2048), (256, 16384)]
+ROPE_GRID = [(8192, 128), (32768, 128), (65536, 64), (16384, 256)]
+
+
+def _eager_table():
+    F = torch.nn.functional
+    C = 0.7978845608028654
+
+    def gelu(t):
+        return 0.5 * t * (1.0 + torch.tanh(C * (t + 0.044715 * t * t * t)))
+
+    def ln(h, w, b):
+        mu = h.mean(-1, keepdim=True)
+        hc = h - mu
+        return hc * torch.rsqrt((hc * hc).mean(-1, keepdim=True) + 1e-5) * w.float() + b.float()
+
+    def rot(xf):
+        h = xf.shape[-1] // 2
+        return torch.cat([-xf[..., h:], xf[..., :h]], -1)
+
+    return {  # the expressions of ouroboros/specs.py / chains.py, eager
+        "rmsnorm": lambda x, w: (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype) * w,
+        "rmsnorm_gemma": lambda x, w: (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6) * (1.0 + w.float())).to(x.dtype),
+        "softmax": lambda x: torch.softmax(x.float(), -1).to(x.dtype),
+        "log_softmax": lambda x: torch.log_softmax(x.float(), -1).to(x.dtype),
+        "softcap_softmax": lambda x: torch.softmax(30.0 * torch.tanh(x.float() / 30.0), -1).to(x.dtype),
+        "swiglu": lambda g, u: (F.silu(g.float()) * u.float()).to(g.dtype),
+        "glu": lambda g, u: (torch.sigmoid(g.float()) * u.float()).to(g.dtype),
+        "geglu": lambda g, u: (gelu(g.float()) * u.float()).to(g.dtype),
+        "gelu": lambda x: gelu(x.float()).to(x.dtype),
+        "silu": lambda x: (x.float() * torch.sigmoid(x.float())).to(x.dtype),
+        "add_rmsnorm": lambda x, r, w: ((x.float() + r.float()) * torch.rsqrt((x.float() + r.float()).pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype) * w,
+        "layernorm": lambda x, w, b: ln(x.float(), w, b).to(x.dtype),
+        "add_layernorm": lambda x, r, w, b: ln(x.float() + r.float(), w, b).to(x.dtype),
+        "layernorm_gelu": lambda x, w, b: gelu(ln(x.float(), w, b)).to(x.dtype),
+        "add_layernorm_gelu": lambda x, r, w, b: gelu(ln(x.float() + r.float(), w, b)).to(x.dtype),
+        "add_rmsnorm_silu": lambda x, r, w: F.silu((x.float() + r.float()) * torch.rsqrt((x.float() + r.float()).pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()).to(x.dtype),
+        "cross_entropy": lambda x, t: F.cross_entropy(x.float(), t, reduction="none").to(x.dtype),
+        "rope": lambda x, c, s: (x.float() * c.float() + rot(x.float()) * s.float()).to(x.dtype),
+        "rope_interleaved": None,
+        "qknorm_rope": None,
+    }
+
+
+GRID_OPS = ["rmsnorm", "rmsnorm_gemma", "softmax", "log_softmax", "softcap_softmax", "swiglu",
+            "glu", "geglu", "gelu", "silu", "add_rmsnorm", "layernorm", "add_layernorm",
+            "layernorm_gelu", "add_layernorm_gelu", "add_rmsnorm_silu", "cross_entropy", "rope",
+            "rope_interleaved", "qknorm_rope"]
+
+
+def _grid_inputs(kind, M, N, dt, device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    rn = lambda *s: torch.randn(s, generator=g, device=device).to(dt)
+    if kind == "x":
+        return (rn(M, N),)
+    if kind in ("rms",):
+        return (rn(M, N), rn(N))
+    if kind == "ln":
+        return (rn(M, N), rn(N), rn(N))
+    if kind == "add_rms":
+        return (rn(M, N), rn(M, N), rn(N))
+    if kind == "add_ln":
+        return (rn(M, N), rn(M, N), rn(N), rn(N))
+    if kind == "gate_up":
+        return (rn(M, N), rn(M, N))
+    if kind == "ce":
+        return (rn(M, N), torch.randint(0, N, (M,), generator=g, device=device))
+    ang = torch.randn((M, N // 2), generator=g, device=device)
+    c, s = ang.cos(), ang.sin()
+    if kind == "rope_inter":
+        return (rn(M, N), c.to(dt), s.to(dt))
+    cos, sin = torch.cat([c, c], -1).to(dt), torch.cat([s, s], -1).to(dt)
+    if kind == "rope":
+        return (rn(M, N), cos, sin)
+    if kind == "qkr":
+        return (rn(M, N), rn(N), cos, sin)
+    raise KeyError(kind)
+
+
+def _algo_bytes(args, out):
+    return sum(t.numel() * t.element_size() for t in args) + out.numel() * out.element_size()
+
+
+def run_grid(args, device):
+    import b200k
+    from oracle import regimes
+    from oracle.numerics import allclose_report, tol_for
+    eager = _eager_table()
+    peak, _ = hbm_peak()
+    stream = torch.cuda.current_stream(device)
+    ops = args.grid.split(",") if args.grid not in ("1", "all") else GRID_OPS
+    tdt = {"fp16": torch.float16, "bf16": torch.bfloat16}
+    odt = {"fp16": "f16", "bf16": "bf16"}
+    for op in ops:
+        kind = regimes.OPS[op].kind
+        cells = ROPE_GRID if kind in ("rope", "rope_inter", "qkr", "arr") else MATRIX_GRID
+        res = []
+        for (M, N) in cells:
+            for dname in ("fp16", "bf16"):
+                inp = _grid_inputs(kind, M, N, tdt[dname], device, 1000 + M + N)
+                run = b200k.get_op(op)
+                out = run(*inp)
+                # parity: 16 sampled rows against the oracle
+                rows = torch.unique(torch.randint(0, M, (16,), generator=torch.Generator().manual_seed(M)))
+                sub = []
+                for t in inp:
+                    v = t.float().cpu().numpy() if t.is_floating_point() else t.cpu().numpy()
+                    if (t.dim() >= 2 and t.shape[0] == M) or (t.dim() == 1 and not t.is_floating_point()):
+                        v = v[rows.numpy()]
+                    tag = odt[dname] if t.is_floating_point() else "i64"
+                    sub.append((v, tag))
+                ref = regimes.reference(op, sub)
+                got = out.float().cpu().numpy()[rows.numpy()]
+                ok = allclose_report(got, ref, *tol_for(op, odt[dname]))[0]
+                ms, _ = time_steps(lambda: run(*inp), 20, stream, graph_steps=10)
+                nbytes = _algo_bytes(inp, out)
+                cell = {"M": M, "N": N, "dtype": dname, "parity": bool(ok),
+                        "us": round(ms * 1e3, 2), "GBs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                        "frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 3)}
+                e = eager.get(op)
+                if e is not None:
+                    e(*inp)
+                    torch.cuda.synchronize()
+                    em, _ = time_steps(lambda: e(*inp), 10, stream, graph_steps=5)
+                    cell["eager_us"] = round(em * 1e3, 2)
+                    cell["speedup_vs_eager"] = round(em / ms, 2)
+                res.append(cell)
+                del inp, out
+        sp = [c["speedup_vs_eager"] for c in res if "speedup_vs_eager" in c]
+        geo = float(np.exp(np.mean(np.log(sp)))) if sp else None
+        print(json.dumps({"op": op, "cells": res, "all_parity": all(c["parity"] for c in res),
+                          "geomean_speedup_vs_eager": round(geo, 3) if geo else None,
+                          "mean_frac": round(float(np.mean([c["frac"] for c in res])), 3)}),
+              flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # device timing
 def time_steps(fn, steps, stream, graph_steps=0):
     """ms per step of fn() over `steps` steps, CUDA events on `stream`.  With
@@ -623,7 +823,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", default="chain", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="chain", choices=sorted(WORKLOADS) + ["mlp_block"])
     ap.add_argument("--impl", default="b200k", choices=["b200k", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
@@ -633,6 +833,8 @@ def main():
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--graph", type=int, default=1,
                     help="launch small workloads from a CUDA graph (1) or one by one (0)")
+    ap.add_argument("--grid", default="",
+                    help="shape-grid mode: comma list of ops (or 'all'); one JSON line per op")
     ap.add_argument("--rows", type=int, default=0,
                     help="override the row count of the workload (M; batch for rope; "
                          "tokens for ce) — small cases for profiler captures")
@@ -642,6 +844,13 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.grid:
+        torch.cuda.set_device(local)
+        sys.path.insert(0, ROOT)
+        sys.exit(run_grid(args, torch.device("cuda", local)))
+    if args.workload == "mlp_block":
+        torch.cuda.set_device(local)
+        sys.exit(run_mlp_block(args, torch.device("cuda", local)))
     wl = WORKLOADS[args.workload]()
     if args.rows > 0:
         wl.set_rows(args.rows)
