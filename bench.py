@@ -426,6 +426,64 @@ class CrossEntropy(Workload):
         return self.V * 2 + 8
 
 
+class CrossEntropyFwdBwd(CrossEntropy):
+    """configs[4] with the gradient: mean CE over valid tokens and
+    d loss / d logits (bf16) in one pass over the logits."""
+    name = "cross_entropy_fwd_bwd"
+    launches_per_step = 4  # valid count, fused fwd+bwd, shard reduce, mean
+
+    def step(self):
+        return self.b2k.cross_entropy_fwd_bwd(self.x, self.t)
+
+    def bytes_per_step(self):
+        rows = self.r1 - self.r0
+        return 2 * rows * self.V * 2 + rows * 8  # logits read once, gradient written once
+
+    def eager_step(self):
+        xf = self.x.float().requires_grad_(True)
+        loss = torch.nn.functional.cross_entropy(xf, self.t, ignore_index=-100)
+        loss.backward()
+        return loss.detach(), xf.grad.to(torch.bfloat16)
+
+    def config(self):
+        c = super().config()
+        c["workload"] = "cross_entropy_fwd_bwd"
+        c["outputs"] = "mean loss (fp32) and d loss / d logits (bf16)"
+        return c
+
+    def e2e_api(self):
+        return ("b200k.cross_entropy_fwd_bwd on a 4096-row slice copied from pinned host memory, "
+                "loss and gradient copied back")
+
+    def e2e_setup(self):
+        h2d, _ = super().e2e_setup()
+        self.hg = torch.empty((self.e2e_rows, self.V), dtype=torch.bfloat16).pin_memory()
+        return h2d, 4 + self.e2e_rows * self.V * 2
+
+    def e2e_bytes(self):
+        return self.e2e_rows * (2 * self.V * 2 + 8)
+
+    def e2e_step(self, timing):
+        cur = torch.cuda.current_stream(self.device)
+        timing[0].record(cur)
+        x = self.hx.to(self.device, non_blocking=True)
+        t = self.ht.to(self.device, non_blocking=True)
+        loss, dx = self.b2k.cross_entropy_fwd_bwd(x, t)
+        host = torch.empty((), dtype=torch.float32, pin_memory=True)
+        host.copy_(loss, non_blocking=True)
+        self.hg.copy_(dx, non_blocking=True)
+        timing[1].record(cur)
+        cur.synchronize()
+
+    def cpu_run(self, r0, r1):
+        from oracle import ops as O
+        return (O.cross_entropy_sum_count(self.cx[r0:r1], self.ct[r0:r1]),
+                O.cross_entropy_grad(self.cx[r0:r1], self.ct[r0:r1], "bf16"))
+
+    def cpu_bytes_per_row(self):
+        return 2 * self.V * 2 + 8
+
+
 class RoPE(Workload):
     """q [8,4096,32,128], k [8,4096,8,128] bf16, positions 0..S-1,
     theta 10000, tables [S, 64] computed in fp32 and cast to bf16; q and k
@@ -519,6 +577,7 @@ class RoPEInterleaved(RoPE):
 
 
 WORKLOADS = {"chain": Chain, "rmsnorm": RMSNorm, "swiglu": SwiGLU, "ce": CrossEntropy,
+             "ce_fwd_bwd": CrossEntropyFwdBwd,
              "rope": RoPE, "rope_interleaved": RoPEInterleaved}
 
 

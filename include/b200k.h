@@ -192,6 +192,25 @@ int b2k_ce_reduce(const float* row_loss, const int64_t* tgt, int64_t M,
 /* out[0] = (float)(sumcount[0] / sumcount[1]) (NaN when the count is 0). */
 int b2k_ce_mean(const double* sumcount, float* out, void* stream);
 
+/* count[0] = number of rows with tgt != ignore_index (fp64, one block). */
+int b2k_ce_valid_count(const int64_t* tgt, int64_t M, int64_t ignore_index,
+                       double* count, void* stream);
+
+/* Forward and backward of the reduced cross-entropy in one kernel: per-row
+ * fp32 losses as b2k_cross_entropy, and the gradient of
+ * grad_scale * mean-over-valid-rows(loss) w.r.t. the logits,
+ *   dx[i, j] = (softmax(x[i])[j] - [j == tgt[i]]) * grad_scale / *valid_count,
+ * 0 for rows with tgt == ignore_index (NaN for other out-of-range targets),
+ * written in dtype with row stride ldd (dx may alias x).  The logits are read
+ * from HBM once: the second pass over a row is served from L2.
+ * valid_count is a device fp64 (b2k_ce_valid_count, all-reduced when rows are
+ * sharded).  The gradient the reference pays for in a separate backward
+ * (ouroboros/README.md:56-58 on the fused Liger kernel). */
+int b2k_cross_entropy_fwd_bwd(const void* x, int64_t ldx, const int64_t* tgt, int64_t M,
+                              int64_t N, int dtype, int64_t ignore_index,
+                              const double* valid_count, float grad_scale, float* row_loss,
+                              void* dx, int64_t ldd, void* stream);
+
 /* Largest M accepted by b2k_cross_entropy_mean_noalloc. */
 #define B2K_NOALLOC_MAX_ROWS 262144
 

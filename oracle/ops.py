@@ -334,3 +334,20 @@ def kl_div(x, y, dt):
         return t - (m + np.log(np.sum(np.exp(t - m), axis=-1, keepdims=True, dtype=np.float32)))
     lx, ly = lsm(_f(x)), lsm(_f(y))
     return rnd(np.sum(np.exp(lx) * (lx - ly), axis=-1, dtype=np.float32), dt)
+
+
+def cross_entropy_grad(x, tgt, dt, grad_scale=1.0, ignore_index=-100):
+    """d(grad_scale * mean over valid rows of cross_entropy(x, t)) / dx, the
+    backward of specs.py:239-241 under a mean reduction: (softmax(x) -
+    onehot(t)) * grad_scale / n_valid, 0 on rows whose target is ignore_index."""
+    xf = _f(x)
+    t = np.asarray(tgt, dtype=np.int64)
+    valid = t != ignore_index
+    n = max(int(valid.sum()), 1)
+    m = np.max(xf, axis=-1, keepdims=True)
+    e = np.exp(xf - m)
+    p = e / np.sum(e, axis=-1, keepdims=True, dtype=np.float32)
+    rows = np.nonzero(valid)[0]
+    p[rows, t[rows]] -= F(1.0)
+    p[~valid] = F(0.0)
+    return rnd(p * F(grad_scale / n), dt)

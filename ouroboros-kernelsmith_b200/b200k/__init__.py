@@ -10,10 +10,10 @@ it is missing the import fails (there is no CPU fallback).
 from . import _lib
 from ._lib import B200KError
 from .ops import *  # noqa: F401,F403
-from .ops import fused_add_norm, norm_chain, rope_qk, cross_entropy_mean  # noqa: F401
+from .ops import fused_add_norm, norm_chain, rope_qk, cross_entropy_mean, cross_entropy_fwd_bwd  # noqa: F401
 from . import dist, host  # noqa: F401
 from .registry import OPS, get_op, candidate_source  # noqa: F401
 
 __all__ = ["OPS", "get_op", "candidate_source", "B200KError", "fused_add_norm", "rope_qk",
-           "cross_entropy_mean", "dist", "host"]
+           "cross_entropy_mean", "cross_entropy_fwd_bwd", "dist", "host"]
 __version__ = "0.1.0"

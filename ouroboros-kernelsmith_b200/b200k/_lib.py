@@ -54,6 +54,10 @@ SIGNATURES = {
                                   c_int, c_int64, c_void_p]),
     "b2k_ce_reduce": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
     "b2k_ce_mean": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "b2k_ce_valid_count": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
+    "b2k_cross_entropy_fwd_bwd": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int,
+                                          c_int64, c_void_p, c_float, c_void_p, c_void_p,
+                                          c_int64, c_void_p]),
     "b2k_cross_entropy_mean_noalloc": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64,
                                                c_int, c_int64, c_void_p, c_void_p]),
     "b2k_cumsum": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int,

@@ -543,3 +543,44 @@ def cross_entropy_mean(logits, tgt, ignore_index: int = -100, group=None):
     with _dev(dev) as stream:
         L.check(L.lib.b2k_ce_mean(_p(sumcount), _p(out), stream), "b2k_ce_mean")
     return out
+
+
+def cross_entropy_fwd_bwd(logits, tgt, ignore_index: int = -100, group=None,
+                          grad_scale: float = 1.0, inplace: bool = False):
+    """Mean cross-entropy over valid rows AND its gradient w.r.t. the logits
+    in one pass over the logits: returns (loss 0-dim fp32, dlogits) with
+    dlogits = grad_scale * d(mean loss)/d logits in the logits' dtype
+    (0 for ignored rows).  With a process group, logits/tgt are this rank's
+    row shard; the valid count and the loss sum are all-reduced (NCCL) so
+    the loss and gradient are those of the global mean.  inplace=True writes
+    the gradient over the logits (the memory-saving form of fused CE)."""
+    from .dist import allreduce_sumcount
+    dev = _cuda(logits, tgt)
+    dt = _dtype_id(logits)
+    n = logits.shape[-1]
+    x2, ldx = _rows(logits, n)
+    m = x2.shape[0]
+    t1 = _check_tgt(tgt, m, dev)
+    if inplace and not (x2.data_ptr() == logits.data_ptr() and logits.is_contiguous()):
+        raise ValueError("b200k: inplace gradient needs contiguous logits")
+    dx = x2 if inplace else torch.empty((m, n), dtype=logits.dtype, device=dev)
+    lddx = ldx if inplace else n
+    count = torch.empty((2,), dtype=torch.float64, device=dev)
+    row_loss = torch.empty((m,), dtype=torch.float32, device=dev)
+    sumcount = torch.empty((2,), dtype=torch.float64, device=dev)
+    out = torch.empty((), dtype=torch.float32, device=dev)
+    with _dev(dev) as stream:
+        L.check(L.lib.b2k_ce_valid_count(_p(t1), m, ignore_index, _p(count), stream),
+                "b2k_ce_valid_count")
+    count[1:].zero_()
+    allreduce_sumcount(count, group)
+    with _dev(dev) as stream:
+        L.check(L.lib.b2k_cross_entropy_fwd_bwd(_p(x2), ldx, _p(t1), m, n, dt, ignore_index,
+                                                _p(count), grad_scale, _p(row_loss), _p(dx),
+                                                lddx, stream), "b2k_cross_entropy_fwd_bwd")
+        L.check(L.lib.b2k_ce_reduce(_p(row_loss), _p(t1), m, ignore_index, _p(sumcount), stream),
+                "b2k_ce_reduce")
+    allreduce_sumcount(sumcount, group)
+    with _dev(dev) as stream:
+        L.check(L.lib.b2k_ce_mean(_p(sumcount), _p(out), stream), "b2k_ce_mean")
+    return out, dx.view(logits.shape)

@@ -32,6 +32,12 @@ struct CeArgs {
   void* loss;
   int64_t ldx, M, N, ignore;
   int aligned;
+  // backward (fused forward + gradient): dx = (softmax(x) - onehot(t)) *
+  // grad_scale / *valid_count for valid rows, 0 for ignored rows
+  void* dx;
+  int64_t ldd;
+  const double* valid_count;
+  float grad_scale;
 };
 
 template <typename T, typename OutT>
@@ -101,7 +107,7 @@ constexpr int kCeChunkBytes = 16384;
 constexpr int kCeConsumerWarps = 8;
 constexpr int kCeThreads = 32 * (kCeConsumerWarps + 1);
 
-template <typename T, typename OutT>
+template <typename T, typename OutT, bool BWD>
 __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, const int S) {
   constexpr int E = Traits<T>::E;
   constexpr int H = E / 2;
@@ -114,6 +120,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
   __shared__ float red_m[kCeConsumerWarps], red_s[kCeConsumerWarps];
   __shared__ volatile int abort_flag;
   __shared__ int stop;
+  __shared__ float row_lse;
   __shared__ int64_t consumed;
   uint64_t* full = reinterpret_cast<uint64_t*>(dsm + (size_t)S * kCeChunkBytes);
   uint64_t* empty = full + S;
@@ -150,7 +157,10 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
       if (t == a.ignore || t < 0 || t >= N) continue;
       const T* xr = xg + row * a.ldx;
       bool ok = true;
-      for (int64_t c = 0; c < nchunks; ++c) {
+      // forward: one pass; with the gradient a second pass over the same
+      // row (served from L2: the row was read a moment ago)
+      for (int64_t cc = 0; cc < (BWD ? 2 : 1) * nchunks; ++cc) {
+        const int64_t c = cc < nchunks ? cc : cc - nchunks;
         const int s = p_stage;
         if (issued >= S) {
           ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], p_phase ^ 1u));
@@ -186,6 +196,15 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
         if (ct == 0)
           static_cast<OutT*>(a.loss)[row] =
               from_f<OutT>(ignore ? 0.0f : __int_as_float(0x7fc00000));
+        if constexpr (BWD) {  // no gradient through ignored rows (NaN for bad targets)
+          const float fill = ignore ? 0.0f : __int_as_float(0x7fc00000);
+          float z[E];
+#pragma unroll
+          for (int e = 0; e < E; ++e) z[e] = fill;
+          const uint4 zv = pack<T>(z);
+          T* dr = static_cast<T*>(a.dx) + row * a.ldd;
+          for (int64_t c = (int64_t)ct * E; c < N; c += (int64_t)NC * E) st_stream(dr + c, zv);
+        }
         continue;
       }
       float m = -INFINITY, s = 0.0f;
@@ -270,10 +289,57 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
         const float lse = M + (P ? logf(Ssum) : f_log<false>(Ssum));
         const float xt = to_f<T>(xg[row * a.ldx + t]);
         static_cast<OutT*>(a.loss)[row] = from_f<OutT>(lse - xt);
+        row_lse = lse;
         stop = abort_flag;
       }
       named_bar_sync(1, NC);
       if (stop) break;
+      if constexpr (BWD) {
+        // second pass: dx = exp(x - lse) * scale - scale * [j == t]
+        const float lse = row_lse;
+        const float scale = a.grad_scale / (float)(*a.valid_count);
+        const float2 nl = f2s(-lse * kLog2e);
+        T* dr = static_cast<T*>(a.dx) + row * a.ldd;
+        int n_left2 = (int)(N < (int64_t)0x7fffffff ? N : 0x7fffffff);
+        for (int64_t c = 0; c < nchunks; ++c, ++u, n_left2 -= CE) {
+          const int st = c_stage;
+          bool ok = false;
+          if (!abort_flag) {
+            ok = mbar_wait(&full[st], c_phase);
+            if (!ok) { abort_flag = 1; atomicAdd(&b2k_tu_timeouts, 1u); }
+          }
+          if (ok) {
+            const T* cs = reinterpret_cast<const T*>(dsm + (size_t)st * kCeChunkBytes);
+            const int n = n_left2 < CE ? n_left2 : CE;
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+              const int idx = (k * NC + ct) * E;
+              if (idx < n) {
+                float2 v[H];
+                unpack2<T>(*reinterpret_cast<const uint4*>(cs + idx), v);
+#pragma unroll
+                for (int j = 0; j < H; ++j) {
+                  if constexpr (P) {
+                    v[j] = f2(expf(v[j].x - lse) * scale, expf(v[j].y - lse) * scale);
+                  } else {
+                    const float2 z = fma2(v[j], f2s(kLog2e), nl);
+                    v[j] = mul2(f2(ex2_approx(z.x), ex2_approx(z.y)), f2s(scale));
+                  }
+                }
+                const int64_t gidx = c * CE + idx;
+                if (t >= gidx && t < gidx + E) {
+                  float* vf = reinterpret_cast<float*>(v);
+                  vf[t - gidx] -= scale;
+                }
+                st_stream(dr + gidx, pack2<T>(v));
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[st]);
+          if (++c_stage == S) { c_stage = 0; c_phase ^= 1u; }
+        }
+      }
     }
     if (ct == 0) consumed = u;
   }
@@ -289,10 +355,13 @@ static int ce_env(const char* name, int dflt) {
   return s ? atoi(s) : dflt;
 }
 
+// Launches the row-loss kernel; with a.dx set, the pipelined kernel also
+// writes the gradient (*bwd_done = true), the rows kernel does not.
 template <typename T, typename OutT>
-static int ce_launch(const CeArgs& a, cudaStream_t st) {
+static int ce_launch(const CeArgs& a, cudaStream_t st, bool* bwd_done = nullptr) {
   constexpr int E = Traits<T>::E;
   static const int use_tma = ce_env("B2K_TMA", 1);
+  if (bwd_done) *bwd_done = false;
   if (use_tma && a.aligned && a.N * (int64_t)sizeof(T) >= 4 * kCeChunkBytes) {
     static const int S = [] {
       const int v = ce_env("B2K_CE_STAGES", 4);
@@ -305,9 +374,10 @@ static int ce_launch(const CeArgs& a, cudaStream_t st) {
     const size_t smem = (size_t)S * kCeChunkBytes + 2 * (size_t)S * sizeof(uint64_t);
     int64_t grid = (int64_t)sm_count() * cps;
     if (grid > a.M) grid = a.M;
-    cudaFuncSetAttribute(ce_tma_kernel<T, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    ce_tma_kernel<T, OutT><<<(unsigned)grid, kCeThreads, smem, st>>>(a, S);
+    auto kern = a.dx ? ce_tma_kernel<T, OutT, true> : ce_tma_kernel<T, OutT, false>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<(unsigned)grid, kCeThreads, smem, st>>>(a, S);
+    if (bwd_done) *bwd_done = a.dx != nullptr;
     return check_launch("b2k_cross_entropy(tma)");
   }
   const int64_t nvec = (a.N + E - 1) / E;
@@ -354,6 +424,47 @@ __global__ void ce_mean_kernel(const double* sumcount, float* out) {
   out[0] = (float)(sumcount[0] / sumcount[1]);  // 0/0 -> NaN (no valid row)
 }
 
+// Gradient of the mean loss for layouts the pipelined kernel does not take
+// (short or misaligned rows): lse recovered from the fp32 row loss
+// (loss = lse - x[t]), then dx = (exp(x - lse) - [j == t]) * scale.
+template <typename T>
+__global__ void __launch_bounds__(256) ce_bwd_rows_kernel(const CeArgs a) {
+  constexpr bool P = std::is_same<T, float>::value;
+  const int64_t row = blockIdx.x;
+  const int64_t t = a.tgt[row];
+  const bool ignore = (t == a.ignore), bad = !ignore && (t < 0 || t >= a.N);
+  const T* xr = static_cast<const T*>(a.x) + row * a.ldx;
+  T* dr = static_cast<T*>(a.dx) + row * a.ldd;
+  if (ignore || bad) {
+    const float fill = ignore ? 0.0f : __int_as_float(0x7fc00000);
+    for (int64_t j = threadIdx.x; j < a.N; j += blockDim.x) dr[j] = from_f<T>(fill);
+    return;
+  }
+  const float lse = static_cast<const float*>(a.loss)[row] + to_f<T>(xr[t]);
+  const float scale = a.grad_scale / (float)(*a.valid_count);
+  for (int64_t j = threadIdx.x; j < a.N; j += blockDim.x) {
+    float d = f_exp<P>(to_f<T>(xr[j]) - lse) * scale;
+    if (j == t) d -= scale;
+    dr[j] = from_f<T>(d);
+  }
+}
+
+__global__ void __launch_bounds__(1024) ce_count_kernel(const int64_t* tgt, int64_t M,
+                                                        int64_t ignore, double* count) {
+  __shared__ double rc[32];
+  double c = 0.0;
+  for (int64_t i = threadIdx.x; i < M; i += blockDim.x) c += (tgt[i] != ignore) ? 1.0 : 0.0;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) rc[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double tc = 0.0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tc += rc[i];
+    *count = tc;
+  }
+}
+
 }  // namespace b2k
 
 using namespace b2k;
@@ -369,7 +480,7 @@ extern "C" int b2k_cross_entropy(const void* x, int64_t ldx, const int64_t* tgt,
   if (M == 0) return B2K_OK;
   B2K_REQUIRE(x != nullptr || N == 0, "b2k_cross_entropy: null x");
   B2K_REQUIRE(tgt != nullptr && loss != nullptr, "b2k_cross_entropy: null tgt/loss");
-  CeArgs a;
+  CeArgs a = {};
   a.x = x; a.tgt = tgt; a.loss = loss; a.ldx = ldx; a.M = M; a.N = N; a.ignore = ignore_index;
   const int es = dtype_size(dtype);
   const int E = es ? 16 / es : 1;
@@ -396,4 +507,41 @@ extern "C" int b2k_ce_mean(const double* sumcount, float* out, void* stream) {
   B2K_REQUIRE(sumcount != nullptr && out != nullptr, "b2k_ce_mean: null pointer");
   ce_mean_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(sumcount, out);
   return check_launch("b2k_ce_mean");
+}
+
+extern "C" int b2k_ce_valid_count(const int64_t* tgt, int64_t M, int64_t ignore_index,
+                                  double* count, void* stream) {
+  B2K_REQUIRE(M >= 0 && count != nullptr && (M == 0 || tgt != nullptr),
+              "b2k_ce_valid_count: bad arguments");
+  ce_count_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(tgt, M, ignore_index, count);
+  return check_launch("b2k_ce_valid_count");
+}
+
+extern "C" int b2k_cross_entropy_fwd_bwd(const void* x, int64_t ldx, const int64_t* tgt,
+                                         int64_t M, int64_t N, int dtype, int64_t ignore_index,
+                                         const double* valid_count, float grad_scale,
+                                         float* row_loss, void* dx, int64_t ldd, void* stream) {
+  B2K_REQUIRE(M >= 0 && N >= 1, "b2k_cross_entropy_fwd_bwd: need M >= 0 and N >= 1");
+  B2K_REQUIRE(M <= 1 || (ldx >= N && ldd >= N), "b2k_cross_entropy_fwd_bwd: row stride < N");
+  B2K_REQUIRE(valid_count != nullptr && row_loss != nullptr && dx != nullptr,
+              "b2k_cross_entropy_fwd_bwd: null valid_count / row_loss / dx");
+  B2K_REQUIRE(M <= 0x7fffffffLL, "b2k_cross_entropy_fwd_bwd: too many rows");
+  if (M == 0) return B2K_OK;
+  CeArgs a = {};
+  a.x = x; a.tgt = tgt; a.loss = row_loss; a.ldx = ldx; a.M = M; a.N = N; a.ignore = ignore_index;
+  a.dx = dx; a.ldd = ldd; a.valid_count = valid_count; a.grad_scale = grad_scale;
+  const int es = dtype_size(dtype);
+  const int E = es ? 16 / es : 1;
+  a.aligned = (N % E == 0) && aligned16(x) && aligned16(dx) && ((ldx * es) % 16 == 0) &&
+              ((ldd * es) % 16 == 0);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  B2K_DISPATCH_FLOAT(dtype, {
+    bool done = false;
+    const int rc = ce_launch<T, float>(a, st, &done);
+    if (rc != B2K_OK || done) return rc;
+    // the rows kernel wrote the row losses; now the gradient from them
+    ce_bwd_rows_kernel<T><<<(unsigned)M, 256, 0, st>>>(a);
+    return check_launch("b2k_cross_entropy_fwd_bwd");
+  });
+  return B2K_OK;
 }
