@@ -79,10 +79,8 @@ __device__ __forceinline__ float2 norm_pair(float2 h, float2 nmu2, float2 rs2, f
   } else if constexpr (MODE == NM_RMS_W) {
     n = mul2(mul2(h, rs2), w);
   } else if constexpr (MODE == NM_RMS_WROUND) {
-    float2 t = mul2(h, rs2);
-    t = f2(round_to<T>(t.x), round_to<T>(t.y));
-    n = mul2(t, w);
-    n = f2(round_to<T>(n.x), round_to<T>(n.y));
+    // T(T(h*rs) * w): the outer rounding is the store's own conversion to T
+    n = mul2(round2<T>(mul2(h, rs2)), w);
   } else if constexpr (MODE == NM_RMS_1PW) {
     n = mul2(mul2(h, rs2), add2(w, f2s(1.0f)));
   } else {

@@ -18,6 +18,7 @@
 #include <stdlib.h>
 
 #include "rowio.cuh"
+#include "rowpipe.cuh"
 #include "tma.cuh"
 
 B2K_DEFINE_TIMEOUT_COUNTER()
@@ -348,6 +349,86 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
   if (threadIdx.x == 0)
     for (int64_t j = consumed; j < issued; ++j)
       mbar_wait(&full[(int)(j % S)], (uint32_t)((j / S) & 1));
+}
+
+// Rows of 4..64 KB (the spec shapes, V up to 32768 at 2 bytes): whole rows
+// through the persistent bulk-copy row pipeline; each thread takes a local
+// (max, sum-exp) over its slice, one block reduction per row, the target
+// logit read from the staged row.
+template <typename T, typename OutT, int V>
+__global__ void __launch_bounds__(512) ce_pipe_kernel(const CeArgs a, const int S_) {
+  constexpr int E = Traits<T>::E;
+  constexpr int H = E / 2;
+  constexpr bool P = std::is_same<T, float>::value;
+  extern __shared__ __align__(128) unsigned char dsm[];
+  __shared__ float red[1024];
+  __shared__ volatile int abort_flag;
+  __shared__ float xt_s;
+  const Group g;
+  const int N = (int)a.N;
+  if (g.tx == 0) abort_flag = 0;
+  RowPipe<1> pipe;
+  const void* srcs[1] = {a.x};
+  const int64_t lds[1] = {a.ldx};
+  pipe.init(dsm, S_, a.M, (uint32_t)N * (uint32_t)sizeof(T), srcs, lds, (int)sizeof(T));
+  int64_t k = 0;
+  for (; k < pipe.nrows; ++k) {
+    bool ok;
+    const T* xs = reinterpret_cast<const T*>(pipe.wait_next(ok));
+    if (!ok) { abort_flag = 1; atomicAdd(&b2k_tu_timeouts, 1u); }
+    const int64_t row = pipe.row_of(k);
+    const int64_t t = a.tgt[row];
+    const bool ignore = (t == a.ignore), bad = !ignore && (t < 0 || t >= N);
+    float m = -INFINITY, s = 0.0f;
+    if (!ignore && !bad) {
+      float2 v[V][H];
+      float bm = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < V; ++q) {
+        const int c = (q * g.G + g.tx) * E;
+        if (c < N) {
+          unpack2<T>(*reinterpret_cast<const uint4*>(xs + c), v[q]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < H; ++j) v[q][j] = f2s(-INFINITY);
+        }
+#pragma unroll
+        for (int j = 0; j < H; ++j) bm = fmaxf(bm, fmaxf(v[q][j].x, v[q][j].y));
+      }
+      if (bm != -INFINITY) {
+        m = bm;
+        if constexpr (P) {
+#pragma unroll
+          for (int q = 0; q < V; ++q)
+#pragma unroll
+            for (int j = 0; j < H; ++j) s += expf(v[q][j].x - m) + expf(v[q][j].y - m);
+        } else {
+          const float2 nz = f2s(-m * kLog2e);
+          float2 acc = f2s(0.0f);
+#pragma unroll
+          for (int q = 0; q < V; ++q)
+#pragma unroll
+            for (int j = 0; j < H; ++j) {
+              const float2 z = fma2(v[q][j], f2s(kLog2e), nz);
+              acc = add2(acc, f2(ex2_approx(z.x), ex2_approx(z.y)));
+            }
+          s = acc.x + acc.y;
+        }
+      }
+      if (g.tx == 0) xt_s = to_f<T>(xs[t]);
+    }
+    group_lse(m, s, g, red);  // barriers: every read of the stage is done
+    if (abort_flag) break;
+    pipe.refill();
+    if (g.tx == 0) {
+      float loss;
+      if (ignore) loss = 0.0f;
+      else if (bad) loss = __int_as_float(0x7fc00000);
+      else loss = (m + (P ? logf(s) : f_log<false>(s))) - xt_s;
+      static_cast<OutT*>(a.loss)[row] = from_f<OutT>(loss);
+    }
+  }
+  pipe.drain(k);
 }
 
 static int ce_env(const char* name, int dflt) {
