@@ -363,6 +363,8 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
   const Group g;  // G = blockDim.x, one row at a time
   const int N = (int)a.N;
   if (g.tx == 0) abort_flag = 0;
+  griddep_launch_dependents();
+  griddep_wait();  // inputs may come from the previous kernel in the stream
   RowPipe<NIN> pipe;
   const void* srcs[2] = {a.x, a.r};
   const int64_t lds[2] = {a.ldx, a.ldr};
@@ -627,7 +629,7 @@ static bool norm_try_tma(const NormArgs& a, cudaStream_t st, int* status) {
   const size_t smem = RowPipe<RESID ? 2 : 1>::smem_bytes(S, a.N * (int64_t)sizeof(T));
   int64_t grid = (int64_t)sms * cps;
   if (grid > a.M) grid = a.M;
-  kern<<<(unsigned)grid, G, smem, st>>>(a, S);
+  launch_pdl(kern, (unsigned)grid, (unsigned)G, smem, st, a, S);
   *status = check_launch("b2k_norm(tma)");
   return true;
 }

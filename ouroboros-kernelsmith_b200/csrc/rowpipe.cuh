@@ -14,6 +14,7 @@
 #pragma once
 
 #include <mutex>
+#include <stdlib.h>
 
 #include "tma.cuh"
 
@@ -115,6 +116,34 @@ struct RowPipe {
 struct PipeShape {
   int cps, S;
 };
+
+// Launch with programmatic dependent launch enabled (B2K_PDL=0 disables it):
+// the kernel's blocks may be scheduled while the previous kernel of the
+// stream drains; the kernel itself calls griddep_wait() before its first
+// global read.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* s = getenv("B2K_PDL");
+    return !(s && s[0] == '0');
+  }();
+  return on;
+}
+
+template <typename Kernel, typename... Args>
+inline void launch_pdl(Kernel kern, unsigned grid, unsigned block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(block, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, args...);
+}
 
 // Raises the kernel's dynamic shared-memory cap once (to the whole per-block
 // maximum); the launch itself asks for what it needs.

@@ -89,6 +89,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Programmatic dependent launch: the kernel may start while the previous
+// kernel in the stream is still finishing; every input read must come after
+// griddep_wait(), which returns once the preceding grid has completed and its
+// writes are visible.  griddep_launch_dependents() lets the next kernel in
+// the stream begin its own launch (its blocks still wait for resources and,
+// before reading, for this grid to finish).
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Host-side registry of per-translation-unit timeout counters.
 using TimeoutReader = unsigned (*)(bool reset);
 void register_timeout_reader(TimeoutReader f);
