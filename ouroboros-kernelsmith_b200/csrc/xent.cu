@@ -122,6 +122,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
   __shared__ volatile int abort_flag;
   __shared__ int stop;
   __shared__ float row_lse;
+  __shared__ float xt_s;
   __shared__ int64_t consumed;
   uint64_t* full = reinterpret_cast<uint64_t*>(dsm + (size_t)S * kCeChunkBytes);
   uint64_t* empty = full + S;
@@ -149,6 +150,9 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
   int p_stage = 0;
   uint32_t p_phase = 0;  // phase of the current lap; the empty wait is for the previous lap
   if (warp == 0) {
+    const uint64_t pol_keep = policy_evict_last(), pol_drop = policy_evict_first();
+    (void)pol_keep;
+    (void)pol_drop;
     // ---- producer warp: the whole warp walks the loop (warp-uniform
     // control flow), lane 0 issues the bulk copies
     for (int64_t i = 0; i < nrows; ++i) {
@@ -174,7 +178,13 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
           const int64_t n = (N - c * CE) < CE ? (N - c * CE) : CE;
           const uint32_t bytes = (uint32_t)(n * (int64_t)sizeof(T));
           mbar_arrive_expect_tx(&full[s], bytes);
-          bulk_g2s(dsm + (size_t)s * kCeChunkBytes, xr + c * CE, bytes, &full[s]);
+          if constexpr (BWD) {
+            // first pass keeps the row in L2 for the second, which drops it
+            bulk_g2s_hint(dsm + (size_t)s * kCeChunkBytes, xr + c * CE, bytes, &full[s],
+                          cc < nchunks ? pol_keep : pol_drop);
+          } else {
+            bulk_g2s(dsm + (size_t)s * kCeChunkBytes, xr + c * CE, bytes, &full[s]);
+          }
         }
         ++issued;
         if (++p_stage == S) { p_stage = 0; p_phase ^= 1u; }
@@ -189,9 +199,15 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
     int64_t u = 0;
     int c_stage = 0;
     uint32_t c_phase = 0;
+    int64_t t_next = nrows > 0 ? a.tgt[first] : 0;
+    // gradient scale, one load per kernel (the count is written before launch)
+    float scale = 0.0f;
+    if constexpr (BWD) scale = a.grad_scale / (float)(*a.valid_count);
+    (void)scale;
     for (int64_t i = 0; i < nrows; ++i) {
       const int64_t row = first + i * stride;
-      const int64_t t = a.tgt[row];
+      const int64_t t = t_next;  // loaded one row ahead
+      if (i + 1 < nrows) t_next = a.tgt[row + stride];
       const bool ignore = (t == a.ignore);
       if (ignore || t < 0 || t >= N) {
         if (ct == 0)
@@ -208,6 +224,12 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
         }
         continue;
       }
+      // where the target logit sits: chunk, offset, and (second pass) the
+      // consumer thread and vector slot that hold it
+      const int64_t t_chunk = t / CE;
+      const int t_in = (int)(t - t_chunk * CE);
+      const int t_owner = (t_in / E) % NC, t_k = (t_in / E) / NC, t_e = t_in % E;
+      (void)t_owner; (void)t_k; (void)t_e;
       float m = -INFINITY, s = 0.0f;
       int n_left = (int)(N < (int64_t)0x7fffffff ? N : 0x7fffffff);
       for (int64_t c = 0; c < nchunks; ++c, ++u, n_left -= CE) {
@@ -220,6 +242,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
         if (ok) {
           const T* cs = reinterpret_cast<const T*>(dsm + (size_t)st * kCeChunkBytes);
           const int n = n_left < CE ? n_left : CE;
+          if (ct == 0 && c == t_chunk) xt_s = to_f<T>(cs[t_in]);  // the target logit
           float2 v[VPT][H];
 #pragma unroll
           for (int k = 0; k < VPT; ++k) {
@@ -288,8 +311,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
         float M = red_m[0], Ssum = red_s[0];
         for (int w = 1; w < kCeConsumerWarps; ++w) lse_merge(M, Ssum, red_m[w], red_s[w]);
         const float lse = M + (P ? logf(Ssum) : f_log<false>(Ssum));
-        const float xt = to_f<T>(xg[row * a.ldx + t]);
-        static_cast<OutT*>(a.loss)[row] = from_f<OutT>(lse - xt);
+        static_cast<OutT*>(a.loss)[row] = from_f<OutT>(lse - xt_s);
         row_lse = lse;
         stop = abort_flag;
       }
@@ -298,7 +320,6 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
       if constexpr (BWD) {
         // second pass: dx = exp(x - lse) * scale - scale * [j == t]
         const float lse = row_lse;
-        const float scale = a.grad_scale / (float)(*a.valid_count);
         const float2 nl = f2s(-lse * kLog2e);
         T* dr = static_cast<T*>(a.dx) + row * a.ldd;
         int n_left2 = (int)(N < (int64_t)0x7fffffff ? N : 0x7fffffff);
@@ -312,6 +333,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
           if (ok) {
             const T* cs = reinterpret_cast<const T*>(dsm + (size_t)st * kCeChunkBytes);
             const int n = n_left2 < CE ? n_left2 : CE;
+            const int hit_k = (c == t_chunk && ct == t_owner) ? t_k : -1;
 #pragma unroll
             for (int k = 0; k < VPT; ++k) {
               const int idx = (k * NC + ct) * E;
@@ -327,12 +349,14 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
                     v[j] = mul2(f2(ex2_approx(z.x), ex2_approx(z.y)), f2s(scale));
                   }
                 }
-                const int64_t gidx = c * CE + idx;
-                if (t >= gidx && t < gidx + E) {
-                  float* vf = reinterpret_cast<float*>(v);
-                  vf[t - gidx] -= scale;
+                if (k == hit_k) {  // unrolled select keeps v in registers
+#pragma unroll
+                  for (int j = 0; j < H; ++j) {
+                    if (2 * j == t_e) v[j].x -= scale;
+                    if (2 * j + 1 == t_e) v[j].y -= scale;
+                  }
                 }
-                st_stream(dr + gidx, pack2<T>(v));
+                st_stream(dr + c * CE + idx, pack2<T>(v));
               }
             }
           }
@@ -444,14 +468,27 @@ static int ce_launch(const CeArgs& a, cudaStream_t st, bool* bwd_done = nullptr)
   static const int use_tma = ce_env("B2K_TMA", 1);
   if (bwd_done) *bwd_done = false;
   if (use_tma && a.aligned && a.N * (int64_t)sizeof(T) >= 4 * kCeChunkBytes) {
-    static const int S = [] {
+    // ring shape measured at 32768 x 128256 bf16: the forward runs best with
+    // 3 CTAs per SM x 4 stages, forward + gradient (twice the stores, the
+    // second pass served from L2) with 2 CTAs per SM x 6 stages
+    static const int S_fwd = [] {
       const int v = ce_env("B2K_CE_STAGES", 4);
       return v >= 2 && v <= 12 ? v : 4;
     }();
-    static const int cps = [] {
+    static const int cps_fwd = [] {
       const int v = ce_env("B2K_CE_CPS", 3);
       return v >= 1 && v <= 4 ? v : 3;
     }();
+    static const int S_bwd = [] {
+      const int v = ce_env("B2K_CE_BWD_STAGES", 6);
+      return v >= 2 && v <= 12 ? v : 6;
+    }();
+    static const int cps_bwd = [] {
+      const int v = ce_env("B2K_CE_BWD_CPS", 2);
+      return v >= 1 && v <= 4 ? v : 2;
+    }();
+    const int S = a.dx ? S_bwd : S_fwd;
+    const int cps = a.dx ? cps_bwd : cps_fwd;
     const size_t smem = (size_t)S * kCeChunkBytes + 2 * (size_t)S * sizeof(uint64_t);
     int64_t grid = (int64_t)sm_count() * cps;
     if (grid > a.M) grid = a.M;
