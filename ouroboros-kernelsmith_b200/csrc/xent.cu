@@ -104,8 +104,14 @@ __global__ void __launch_bounds__(1024) ce_rows_kernel(const CeArgs a) {
   }
 }
 
-constexpr int kCeChunkBytes = 16384;
-constexpr int kCeConsumerWarps = 8;
+#ifndef B2K_CE_CHUNK_BYTES
+#define B2K_CE_CHUNK_BYTES 16384
+#endif
+#ifndef B2K_CE_CONSUMER_WARPS
+#define B2K_CE_CONSUMER_WARPS 8
+#endif
+constexpr int kCeChunkBytes = B2K_CE_CHUNK_BYTES;
+constexpr int kCeConsumerWarps = B2K_CE_CONSUMER_WARPS;
 constexpr int kCeThreads = 32 * (kCeConsumerWarps + 1);
 
 template <typename T, typename OutT, bool BWD>
@@ -228,8 +234,8 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
       // consumer thread and vector slot that hold it
       const int64_t t_chunk = t / CE;
       const int t_in = (int)(t - t_chunk * CE);
-      const int t_owner = (t_in / E) % NC, t_k = (t_in / E) / NC, t_e = t_in % E;
-      (void)t_owner; (void)t_k; (void)t_e;
+      const int t_owner = (t_in / E) % NC;
+      (void)t_owner;
       float m = -INFINITY, s = 0.0f;
       int n_left = (int)(N < (int64_t)0x7fffffff ? N : 0x7fffffff);
       for (int64_t c = 0; c < nchunks; ++c, ++u, n_left -= CE) {
@@ -244,54 +250,78 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
           const int n = n_left < CE ? n_left : CE;
           if (ct == 0 && c == t_chunk) xt_s = to_f<T>(cs[t_in]);  // the target logit
           float2 v[VPT][H];
+          if (n == CE) {  // every chunk but a row's last: no bounds checks
 #pragma unroll
-          for (int k = 0; k < VPT; ++k) {
-            const int idx = (k * NC + ct) * E;
-            if (idx < n) {
-              unpack2<T>(*reinterpret_cast<const uint4*>(cs + idx), v[k]);
-            } else {
+            for (int k = 0; k < VPT; ++k)
+              unpack2<T>(*reinterpret_cast<const uint4*>(cs + (k * NC + ct) * E), v[k]);
+          } else {
 #pragma unroll
-              for (int j = 0; j < H; ++j) v[k][j] = f2s(-INFINITY);
-            }
-          }
-          // tree max (short dependency chains)
-          float bmk[VPT];
+            for (int k = 0; k < VPT; ++k) {
+              const int idx = (k * NC + ct) * E;
+              if (idx < n) {
+                unpack2<T>(*reinterpret_cast<const uint4*>(cs + idx), v[k]);
+              } else {
 #pragma unroll
-          for (int k = 0; k < VPT; ++k) {
-            float t0 = fmaxf(v[k][0].x, v[k][0].y);
-#pragma unroll
-            for (int j = 1; j < H; ++j) t0 = fmaxf(t0, fmaxf(v[k][j].x, v[k][j].y));
-            bmk[k] = t0;
-          }
-          float bm = bmk[0];
-#pragma unroll
-          for (int k = 1; k < VPT; ++k) bm = fmaxf(bm, bmk[k]);
-          const float nm = fmaxf(m, bm);
-          if (nm != -INFINITY) {
-            if constexpr (P) {
-              float acc = s * expf(m - nm);
-#pragma unroll
-              for (int k = 0; k < VPT; ++k)
-#pragma unroll
-                for (int j = 0; j < H; ++j) acc += expf(v[k][j].x - nm) + expf(v[k][j].y - nm);
-              s = acc;
-            } else {
-              const float2 nz = f2s(-nm * kLog2e);
-              float2 acc[VPT];
-#pragma unroll
-              for (int k = 0; k < VPT; ++k) {
-                acc[k] = f2s(0.0f);
-#pragma unroll
-                for (int j = 0; j < H; ++j) {
-                  const float2 z = fma2(v[k][j], f2s(kLog2e), nz);
-                  acc[k] = add2(acc[k], f2(ex2_approx(z.x), ex2_approx(z.y)));
-                }
+                for (int j = 0; j < H; ++j) v[k][j] = f2s(-INFINITY);
               }
-#pragma unroll
-              for (int k = 1; k < VPT; ++k) acc[0] = add2(acc[0], acc[k]);
-              s = fmaf(s, ex2_approx((m - nm) * kLog2e), acc[0].x + acc[0].y);
             }
-            m = nm;
+          }
+          // sum of 2^(x log2e - nz) over the chunk, f32x2 FMA + ex2.approx
+          auto sum_exp = [&](const float2 nz) {
+            float2 acc[VPT];
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+              acc[k] = f2s(0.0f);
+#pragma unroll
+              for (int j = 0; j < H; ++j) {
+                const float2 z = fma2(v[k][j], f2s(kLog2e), nz);
+                acc[k] = add2(acc[k], f2(ex2_approx(z.x), ex2_approx(z.y)));
+              }
+            }
+#pragma unroll
+            for (int k = 1; k < VPT; ++k) acc[0] = add2(acc[0], acc[k]);
+            return acc[0].x + acc[0].y;
+          };
+          bool done = false;
+          if constexpr (!P) {
+            // Lazy rescale: sum against the running maximum without taking
+            // the chunk's maximum.  A partial sum below 2^64 proves every
+            // term finite and below 2^64 (no rescale needed: the pair stays
+            // exact up to fp32 rounding); otherwise (a new maximum far above
+            // the old one, inf or NaN) the chunk is redone below against its
+            // own maximum.
+            if (m != -INFINITY) {
+              const float part = sum_exp(f2s(-m * kLog2e));
+              if (part < 0x1p64f) { s += part; done = true; }
+            }
+          }
+          if (!done) {
+            // tree max (short dependency chains)
+            float bmk[VPT];
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+              float t0 = fmaxf(v[k][0].x, v[k][0].y);
+#pragma unroll
+              for (int j = 1; j < H; ++j) t0 = fmaxf(t0, fmaxf(v[k][j].x, v[k][j].y));
+              bmk[k] = t0;
+            }
+            float bm = bmk[0];
+#pragma unroll
+            for (int k = 1; k < VPT; ++k) bm = fmaxf(bm, bmk[k]);
+            const float nm = fmaxf(m, bm);
+            if (nm != -INFINITY) {
+              if constexpr (P) {
+                float acc = s * expf(m - nm);
+#pragma unroll
+                for (int k = 0; k < VPT; ++k)
+#pragma unroll
+                  for (int j = 0; j < H; ++j) acc += expf(v[k][j].x - nm) + expf(v[k][j].y - nm);
+                s = acc;
+              } else {
+                s = fmaf(s, ex2_approx((m - nm) * kLog2e), sum_exp(f2s(-nm * kLog2e)));
+              }
+              m = nm;
+            }
           }
         }
         __syncwarp();
@@ -333,31 +363,34 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
           if (ok) {
             const T* cs = reinterpret_cast<const T*>(dsm + (size_t)st * kCeChunkBytes);
             const int n = n_left2 < CE ? n_left2 : CE;
-            const int hit_k = (c == t_chunk && ct == t_owner) ? t_k : -1;
+            auto grad_vec = [&](const int idx) {
+              float2 v[H];
+              unpack2<T>(*reinterpret_cast<const uint4*>(cs + idx), v);
 #pragma unroll
-            for (int k = 0; k < VPT; ++k) {
-              const int idx = (k * NC + ct) * E;
-              if (idx < n) {
-                float2 v[H];
-                unpack2<T>(*reinterpret_cast<const uint4*>(cs + idx), v);
-#pragma unroll
-                for (int j = 0; j < H; ++j) {
-                  if constexpr (P) {
-                    v[j] = f2(expf(v[j].x - lse) * scale, expf(v[j].y - lse) * scale);
-                  } else {
-                    const float2 z = fma2(v[j], f2s(kLog2e), nl);
-                    v[j] = mul2(f2(ex2_approx(z.x), ex2_approx(z.y)), f2s(scale));
-                  }
+              for (int j = 0; j < H; ++j) {
+                if constexpr (P) {
+                  v[j] = f2(expf(v[j].x - lse) * scale, expf(v[j].y - lse) * scale);
+                } else {
+                  const float2 z = fma2(v[j], f2s(kLog2e), nl);
+                  v[j] = mul2(f2(ex2_approx(z.x), ex2_approx(z.y)), f2s(scale));
                 }
-                if (k == hit_k) {  // unrolled select keeps v in registers
-#pragma unroll
-                  for (int j = 0; j < H; ++j) {
-                    if (2 * j == t_e) v[j].x -= scale;
-                    if (2 * j + 1 == t_e) v[j].y -= scale;
-                  }
-                }
-                st_stream(dr + c * CE + idx, pack2<T>(v));
               }
+              st_stream(dr + c * CE + idx, pack2<T>(v));
+            };
+            if (n == CE) {  // full chunk: no bounds checks
+#pragma unroll
+              for (int k = 0; k < VPT; ++k) grad_vec((k * NC + ct) * E);
+            } else {
+#pragma unroll
+              for (int k = 0; k < VPT; ++k)
+                if ((k * NC + ct) * E < n) grad_vec((k * NC + ct) * E);
+            }
+            if (c == t_chunk && ct == t_owner) {
+              // the target's entry, p*scale - scale, stored over the vector
+              // that this same thread wrote above (program order: this wins)
+              const float xt = to_f<T>(cs[t_in]);
+              const float p = P ? expf(xt - lse) : ex2_approx(fmaf(xt, kLog2e, nl.x));
+              dr[t] = from_f<T>(p * scale - scale);
             }
           }
           __syncwarp();

@@ -192,3 +192,23 @@ def test_candidate_imports_like_the_harness(tmp_path):
     assert not torch.equal(y1, y2)
     torch.cuda.synchronize()
     assert _lib.lib.b2k_pipeline_timeouts(1) == 0
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_cross_entropy_nonfinite_logits_give_nan(dt):
+    """A NaN or +inf logit anywhere in a row makes that row's loss NaN, as in
+    F.cross_entropy (checked on CPU: all three rows NaN), in the first chunk of
+    a row, a later one, and the last."""
+    V = 40000  # long enough for the pipelined kernel
+    x = torch.zeros(6, V, dtype=dt, device="cuda")
+    x[0, 8] = float("nan")
+    x[1, 20013] = float("nan")
+    x[2, 16] = float("inf")
+    x[3, V - 1] = float("nan")
+    x[4, 39001] = float("inf")
+    tgt = torch.tensor([1, 1, 1, 1, 1, 2], device="cuda")
+    loss = b200k.cross_entropy(x, tgt).float().cpu()
+    assert torch.isnan(loss[:5]).all(), loss
+    assert abs(float(loss[5]) - float(np.log(V))) < 2e-2 * float(np.log(V))
+    _, g = b200k.cross_entropy_fwd_bwd(x, tgt)
+    assert torch.isnan(g[0].float()).any() and torch.isfinite(g[5].float()).all()
