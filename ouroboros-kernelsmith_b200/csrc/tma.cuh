@@ -99,41 +99,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// try_wait with a suspend-time hint: a thread whose phase is not complete
-// sleeps until it completes or about `hint_ns` pass, instead of returning at
-// once, so waiting warps do not take issue slots from working ones.
-__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity,
-                                                   uint32_t hint_ns) {
-  uint32_t done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return done != 0;
-}
-
-#ifndef B2K_MBAR_SUSPEND_NS
-#define B2K_MBAR_SUSPEND_NS 0
-#endif
-
 // Bounded wait for the phase with `parity` to complete.  Returns false
 // after `limit_ns` of global time without completion.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           unsigned long long limit_ns = kTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
-  if constexpr (B2K_MBAR_SUSPEND_NS > 0) {
-    for (;;) {
-      if (mbar_try_wait_hint(bar, parity, B2K_MBAR_SUSPEND_NS)) return true;
-      if (globaltimer() - t0 > limit_ns) return false;
-    }
-  } else {
-    for (uint32_t i = 1;; ++i) {
-      if (mbar_try_wait(bar, parity)) return true;
-      if ((i & 255u) == 0 && globaltimer() - t0 > limit_ns) return false;
-    }
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer() - t0 > limit_ns) return false;
   }
 }
 

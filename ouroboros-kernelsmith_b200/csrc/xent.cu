@@ -171,7 +171,9 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
       // forward: one pass; with the gradient a second pass over the same
       // row (served from L2: the row was read a moment ago)
       for (int64_t cc = 0; cc < (BWD ? 2 : 1) * nchunks; ++cc) {
-        const int64_t c = cc < nchunks ? cc : cc - nchunks;
+        // the second pass walks the row back to front: its first chunks are
+        // the ones the first pass brought into L2 last
+        const int64_t c = cc < nchunks ? cc : 2 * nchunks - 1 - cc;
         const int s = p_stage;
         if (issued >= S) {
           ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], p_phase ^ 1u));
@@ -352,8 +354,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
         const float lse = row_lse;
         const float2 nl = f2s(-lse * kLog2e);
         T* dr = static_cast<T*>(a.dx) + row * a.ldd;
-        int n_left2 = (int)(N < (int64_t)0x7fffffff ? N : 0x7fffffff);
-        for (int64_t c = 0; c < nchunks; ++c, ++u, n_left2 -= CE) {
+        for (int64_t c = nchunks - 1; c >= 0; --c, ++u) {  // back to front
           const int st = c_stage;
           bool ok = false;
           if (!abort_flag) {
@@ -362,7 +363,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
           }
           if (ok) {
             const T* cs = reinterpret_cast<const T*>(dsm + (size_t)st * kCeChunkBytes);
-            const int n = n_left2 < CE ? n_left2 : CE;
+            const int n = (int)((N - c * CE) < CE ? (N - c * CE) : CE);
             auto grad_vec = [&](const int idx) {
               float2 v[H];
               unpack2<T>(*reinterpret_cast<const uint4*>(cs + idx), v);
@@ -503,7 +504,8 @@ static int ce_launch(const CeArgs& a, cudaStream_t st, bool* bwd_done = nullptr)
   if (use_tma && a.aligned && a.N * (int64_t)sizeof(T) >= 4 * kCeChunkBytes) {
     // ring shape measured at 32768 x 128256 bf16: the forward runs best with
     // 3 CTAs per SM x 4 stages, forward + gradient (twice the stores, the
-    // second pass served from L2) with 2 CTAs per SM x 6 stages
+    // second pass served from L2, whose capacity bounds the rows in flight)
+    // with 2 CTAs per SM x 4 stages
     static const int S_fwd = [] {
       const int v = ce_env("B2K_CE_STAGES", 4);
       return v >= 2 && v <= 12 ? v : 4;
@@ -513,8 +515,8 @@ static int ce_launch(const CeArgs& a, cudaStream_t st, bool* bwd_done = nullptr)
       return v >= 1 && v <= 4 ? v : 3;
     }();
     static const int S_bwd = [] {
-      const int v = ce_env("B2K_CE_BWD_STAGES", 6);
-      return v >= 2 && v <= 12 ? v : 6;
+      const int v = ce_env("B2K_CE_BWD_STAGES", 4);
+      return v >= 2 && v <= 12 ? v : 4;
     }();
     static const int cps_bwd = [] {
       const int v = ce_env("B2K_CE_BWD_CPS", 2);

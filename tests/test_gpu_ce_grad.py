@@ -2,7 +2,9 @@
 mean loss and d(mean loss)/d logits against the CPU oracle (softmax minus
 one-hot over the valid-row count) on the pipelined path (long rows) and the
 row-kernel path (short / odd rows), in place and out of place, plus one
-check against torch autograd in fp32."""
+check against torch autograd in fp32.  301 rows give every persistent block
+a second row, 3 rows leave most blocks idle, and 40000-wide rows end in a
+partial chunk (the first chunk of the back-to-front gradient pass)."""
 import numpy as np
 import pytest
 import torch
@@ -17,7 +19,8 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("dt", ["bf16", "f16", "f32"])
-@pytest.mark.parametrize("shape", [(37, 4097), (96, 1000), (24, 128256), (8, 65536)])
+@pytest.mark.parametrize("shape", [(37, 4097), (96, 1000), (24, 128256), (8, 65536),
+                                   (301, 40000), (3, 40000)])
 @pytest.mark.parametrize("inplace", [False, True])
 def test_fwd_bwd_against_oracle(dt, shape, inplace):
     M, V = shape
