@@ -212,6 +212,11 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
     float scale = 0.0f;
     if constexpr (BWD) scale = a.grad_scale / (float)(*a.valid_count);
     (void)scale;
+    // a positive finite scale is folded into the exponent of the 16-bit path
+    const bool fold = !P && scale > 0.0f && scale < INFINITY;
+    const float log2_scale = fold ? log2f(scale) : 0.0f;
+    (void)fold;
+    (void)log2_scale;
     for (int64_t i = 0; i < nrows; ++i) {
       const int64_t row = first + i * stride;
       const int64_t t = t_next;  // loaded one row ahead
@@ -352,7 +357,9 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
       if constexpr (BWD) {
         // second pass: dx = exp(x - lse) * scale - scale * [j == t]
         const float lse = row_lse;
-        const float2 nl = f2s(-lse * kLog2e);
+        // 16-bit path: exp(x - lse) * scale = 2^(x log2e - lse log2e + log2 scale),
+        // the scale folded into the exponent (one multiply less per pair)
+        const float2 nl = f2s(-lse * kLog2e + (fold ? log2_scale : 0.0f));
         T* dr = static_cast<T*>(a.dx) + row * a.ldd;
         for (int64_t c = nchunks - 1; c >= 0; --c, ++u) {  // back to front
           const int st = c_stage;
@@ -364,7 +371,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
           if (ok) {
             const T* cs = reinterpret_cast<const T*>(dsm + (size_t)st * kCeChunkBytes);
             const int n = (int)((N - c * CE) < CE ? (N - c * CE) : CE);
-            auto grad_vec = [&](const int idx) {
+            auto grad_vec = [&](const int idx, auto folded) {
               float2 v[H];
               unpack2<T>(*reinterpret_cast<const uint4*>(cs + idx), v);
 #pragma unroll
@@ -373,25 +380,33 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
                   v[j] = f2(expf(v[j].x - lse) * scale, expf(v[j].y - lse) * scale);
                 } else {
                   const float2 z = fma2(v[j], f2s(kLog2e), nl);
-                  v[j] = mul2(f2(ex2_approx(z.x), ex2_approx(z.y)), f2s(scale));
+                  v[j] = f2(ex2_approx(z.x), ex2_approx(z.y));
+                  if constexpr (!decltype(folded)::value) v[j] = mul2(v[j], f2s(scale));
                 }
               }
               st_stream(dr + c * CE + idx, pack2<T>(v));
             };
-            if (n == CE) {  // full chunk: no bounds checks
+            auto grad_chunk = [&](auto folded) {
+              if (n == CE) {  // full chunk: no bounds checks
 #pragma unroll
-              for (int k = 0; k < VPT; ++k) grad_vec((k * NC + ct) * E);
-            } else {
+                for (int k = 0; k < VPT; ++k) grad_vec((k * NC + ct) * E, folded);
+              } else {
 #pragma unroll
-              for (int k = 0; k < VPT; ++k)
-                if ((k * NC + ct) * E < n) grad_vec((k * NC + ct) * E);
-            }
+                for (int k = 0; k < VPT; ++k)
+                  if ((k * NC + ct) * E < n) grad_vec((k * NC + ct) * E, folded);
+              }
+            };
+            if (fold) grad_chunk(std::true_type{});
+            else grad_chunk(std::false_type{});
             if (c == t_chunk && ct == t_owner) {
               // the target's entry, p*scale - scale, stored over the vector
               // that this same thread wrote above (program order: this wins)
               const float xt = to_f<T>(cs[t_in]);
-              const float p = P ? expf(xt - lse) : ex2_approx(fmaf(xt, kLog2e, nl.x));
-              dr[t] = from_f<T>(p * scale - scale);
+              float ps;  // p * scale
+              if constexpr (P) ps = expf(xt - lse) * scale;
+              else ps = fold ? ex2_approx(fmaf(xt, kLog2e, nl.x))
+                             : ex2_approx(fmaf(xt, kLog2e, nl.x)) * scale;
+              dr[t] = from_f<T>(ps - scale);
             }
           }
           __syncwarp();

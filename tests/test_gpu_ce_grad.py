@@ -58,3 +58,19 @@ def test_fwd_bwd_matches_autograd():
     got = dx.float() * n_valid
     want = xf.grad * n_valid
     assert torch.allclose(got, want, rtol=2e-2, atol=8e-3), float((got - want).abs().max())
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("grad_scale", [-3.0, 0.0])
+def test_fwd_bwd_nonpositive_grad_scale(dt, grad_scale):
+    """A positive scale is folded into the exponent of the 16-bit gradient
+    pass; zero and negative scales take the plain multiply."""
+    M, V = 24, 128256
+    case = regimes.make_case("ce", 23, M, V, dt, 3.0, ignore_frac=0.1)
+    x, t = to_cuda(case)
+    tn = case[1][0].astype(np.int64)
+    n_valid = int((tn != -100).sum())
+    _, dx = b200k.cross_entropy_fwd_bwd(x, t, grad_scale=grad_scale * n_valid)
+    ref = O.cross_entropy_grad(case[0][0], tn, dt, grad_scale=grad_scale * n_valid)
+    ok, err, bad = allclose_report(dx.float().cpu().numpy(), ref, *tol_for("cross_entropy", dt))
+    assert ok, f"max err {err}, {bad} bad"
