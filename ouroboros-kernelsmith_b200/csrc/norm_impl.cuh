@@ -616,15 +616,23 @@ static bool norm_try_tma(const NormArgs& a, cudaStream_t st, int* status) {
   if (stage > (64 << 10)) return false;
   int G = a.tma_threads;
   if (G <= 0) {
-    G = next_pow2((nvec + 3) / 4);
+    // RMS / L2: two vectors per thread while that fits 256 threads (rows of
+    // <= 512 vectors: more warps per row, fewer registers), else four.
+    // LayerNorm (a costlier block reduction per row): four.
+    G = MODE == NM_LN ? 1 << 30 : next_pow2((nvec + 1) / 2);
+    if (G > 256) G = next_pow2((nvec + 3) / 4);
     G = G < 64 ? 64 : (G > kNormMaxThreads ? kNormMaxThreads : G);
   }
   const int64_t vneed = (nvec + G - 1) / G;
   if (vneed > 4) return false;  // longer rows: register / streaming kernels
   const int sms = sm_count();
   auto kern = (vneed <= 2) ? norm_tma_kernel<T, 2, RESID, MODE, ACT> : norm_tma_kernel<T, 4, RESID, MODE, ACT>;
+  // few rows per SM (a launch of a few microseconds): a 2-stage ring lets more
+  // blocks start at once; the ramp, not the steady state, sets the time
+  int want_stages = a.tma_stages;
+  if (MODE != NM_LN && want_stages <= 0 && a.M <= 32 * (int64_t)sms) want_stages = 2;
   PipeShape ps;
-  if (!choose_pipe_shape(kern, G, stage, a.tma_cps, a.tma_stages, &ps)) return false;
+  if (!choose_pipe_shape(kern, G, stage, a.tma_cps, want_stages, &ps)) return false;
   const int cps = ps.cps, S = ps.S;
   const size_t smem = RowPipe<RESID ? 2 : 1>::smem_bytes(S, a.N * (int64_t)sizeof(T));
   int64_t grid = (int64_t)sms * cps;

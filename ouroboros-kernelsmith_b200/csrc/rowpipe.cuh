@@ -170,8 +170,8 @@ template <typename Kernel>
 inline bool choose_pipe_shape_uncached(Kernel kern, int threads, int64_t stage_bytes,
                                        int want_cps, int want_stages, PipeShape* ps) {
   const int64_t budget = 200 << 10;  // dynamic shared memory per SM
-  if (want_cps > 0 || want_stages > 0) {
-    int cps = want_cps > 0 ? want_cps : 2;
+  if (want_cps > 0) {
+    int cps = want_cps;
     int S = want_stages > 0 ? want_stages : 4;
     while (S > 2 && (int64_t)cps * S * stage_bytes > budget) --S;
     while (cps > 1 && (int64_t)cps * S * stage_bytes > budget) --cps;
@@ -180,8 +180,9 @@ inline bool choose_pipe_shape_uncached(Kernel kern, int threads, int64_t stage_b
     ps->S = S;
     return true;
   }
+  // blocks per SM: as many as are resident, each with want_stages (else 4)
   for (int cps = 8; cps >= 1; --cps) {
-    int S = 4;
+    int S = want_stages > 0 ? want_stages : 4;
     while (S > 2 && (int64_t)cps * S * stage_bytes > budget) --S;
     if ((int64_t)cps * S * stage_bytes > budget) continue;
     const size_t smem = (size_t)S * (size_t)stage_bytes + (size_t)S * sizeof(uint64_t);
