@@ -720,6 +720,8 @@ def _grid_inputs(kind, M, N, dt, device, seed):
         return (rn(M, N), cos, sin)
     if kind == "qkr":
         return (rn(M, N), rn(N), cos, sin)
+    if kind == "arr":
+        return (rn(M, N), rn(M, N), rn(N), cos, sin)
     raise KeyError(kind)
 
 
