@@ -549,6 +549,31 @@ static int ce_launch(const CeArgs& a, cudaStream_t st, bool* bwd_done = nullptr)
     return check_launch("b2k_cross_entropy(tma)");
   }
   const int64_t nvec = (a.N + E - 1) / E;
+  // few rows (<= 8 per SM) of 256 vectors .. 64 KB: whole rows through the
+  // persistent row pipeline, whose staged loads hide the latency a handful of
+  // row blocks cannot (forward only; a gradient is added by the rows kernel).
+  // With more rows the rows kernel below keeps more loads in flight and is
+  // faster (measured on the spec shape grid: 1024 x 4096 5.0 vs 7.2 us,
+  // 8192 x 4096 21.2 vs 18.3 us).
+  static const int use_pipe = ce_env("B2K_CE_PIPE", 1);
+  const int64_t row_bytes = a.N * (int64_t)sizeof(T);
+  if (use_tma && use_pipe && a.aligned && nvec >= 256 && row_bytes <= (64 << 10) &&
+      a.M <= 8 * (int64_t)sm_count()) {
+    int G = next_pow2((nvec + 3) / 4);
+    G = G < 64 ? 64 : (G > 512 ? 512 : G);
+    const int64_t vneed = (nvec + G - 1) / G;
+    if (vneed <= 4) {
+      auto kern = vneed <= 2 ? ce_pipe_kernel<T, OutT, 2> : ce_pipe_kernel<T, OutT, 4>;
+      PipeShape ps;
+      if (choose_pipe_shape(kern, G, row_bytes, 0, 0, &ps)) {
+        const size_t smem = RowPipe<1>::smem_bytes(ps.S, row_bytes);
+        int64_t grid = (int64_t)sm_count() * ps.cps;
+        if (grid > a.M) grid = a.M;
+        kern<<<(unsigned)grid, G, smem, st>>>(a, ps.S);
+        return check_launch("b2k_cross_entropy(pipe)");
+      }
+    }
+  }
   // threads per row: enough that each walks ~32 vectors, 32..1024
   int G = next_pow2((nvec + 31) / 32);
   G = G < 32 ? 32 : (G > 1024 ? 1024 : G);
