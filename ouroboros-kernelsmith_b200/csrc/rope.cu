@@ -333,6 +333,75 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(const NormRopeArgs a) {
   }
 }
 
+// Rows whose half (D/2) is P vectors, P a power of two <= 32 (D = 128 at 16
+// bits: P = 8), 16-byte aligned: a group of P lanes per row inside one warp;
+// lane j holds vector j of BOTH halves of x, w, cos and sin.  RoPE pairs
+// element i with i + D/2, so every lane owns both partners of its rotations:
+// no shared-memory exchange and no block barrier, the row's sum of squares is
+// a log2(P)-step shuffle reduction, and all eight loads of a lane are in
+// flight together.
+template <typename T, bool RESID>
+__global__ void __launch_bounds__(256) norm_rope_half_kernel(const NormRopeArgs a, const int P) {
+  constexpr int E = Traits<T>::E;
+  const int h = a.D / 2;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t row = gid / P;
+  const int c = (int)(gid - row * P) * E;  // offset in the first half
+  const bool valid = row < a.M;
+  // raw 16-byte vectors: the operands used after the reduction stay packed
+  uint4 xv1 = zero4(), xv2 = zero4(), wv1, wv2, cv1, cv2, sv1, sv2;
+  if (valid) {
+    const T* xr = static_cast<const T*>(a.x) + row * a.ldx;
+    const T* cr = static_cast<const T*>(a.cos) + row * a.ldc;
+    const T* sr = static_cast<const T*>(a.sin) + row * a.lds;
+    const T* w = static_cast<const T*>(a.w);
+    xv1 = ld_stream(xr + c);
+    xv2 = ld_stream(xr + c + h);
+    wv1 = ld_keep(w + c);
+    wv2 = ld_keep(w + c + h);
+    cv1 = ld_stream(cr + c);
+    cv2 = ld_stream(cr + c + h);
+    sv1 = ld_stream(sr + c);
+    sv2 = ld_stream(sr + c + h);
+  }
+  float x1[E], x2[E];
+  unpack<T>(xv1, x1);
+  unpack<T>(xv2, x2);
+  if constexpr (RESID) {
+    if (valid) {
+      const T* rr = static_cast<const T*>(a.r) + row * a.ldr;
+      float r1[E], r2[E];
+      unpack<T>(ld_stream(rr + c), r1);
+      unpack<T>(ld_stream(rr + c + h), r2);
+#pragma unroll
+      for (int e = 0; e < E; ++e) { x1[e] += r1[e]; x2[e] += r2[e]; }
+    }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) ss = fmaf(x2[e], x2[e], fmaf(x1[e], x1[e], ss));
+  // the row's P lanes are aligned within the warp: xor offsets < P stay inside
+  for (int o = P >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (!valid) return;
+  const float rs = rsqrtf(ss / (float)a.D + a.eps);
+  float w1[E], w2[E], c1[E], c2[E], s1[E], s2[E], o1[E], o2[E];
+  unpack<T>(wv1, w1);
+  unpack<T>(wv2, w2);
+  unpack<T>(cv1, c1);
+  unpack<T>(cv2, c2);
+  unpack<T>(sv1, s1);
+  unpack<T>(sv2, s2);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float n1 = x1[e] * rs * w1[e], n2 = x2[e] * rs * w2[e];
+    o1[e] = n1 * c1[e] + (-n2) * s1[e];
+    o2[e] = n2 * c2[e] + n1 * s2[e];
+  }
+  T* yr = static_cast<T*>(a.y) + row * a.ldy;
+  st_stream(yr + c, pack<T>(o1));
+  st_stream(yr + c + h, pack<T>(o2));
+}
+
 static unsigned grid_for(int64_t items) {
   const int64_t want = (items + kRopeThreads - 1) / kRopeThreads;
   const int64_t cap = (int64_t)sm_count() * 32;
@@ -459,7 +528,19 @@ extern "C" int b2k_norm_rope(const void* x, int64_t ldx, const void* r, int64_t 
   if (r) al = al && aligned16(r) && (ldr * es) % 16 == 0;
   a.aligned = al ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  static const int use_half = [] {
+    const char* s = getenv("B2K_NORM_ROPE_HALF");
+    return s ? atoi(s) : 1;
+  }();
   B2K_DISPATCH_FLOAT(dtype, {
+    const int P = (int)(D / 2 / Traits<T>::E);
+    if (use_half && al && (D / 2) % Traits<T>::E == 0 && P >= 1 && P <= 32 && (P & (P - 1)) == 0) {
+      const int64_t threads = M * P;
+      const int64_t grid = (threads + 255) / 256;
+      if (r) norm_rope_half_kernel<T, true><<<(unsigned)grid, 256, 0, st>>>(a, P);
+      else norm_rope_half_kernel<T, false><<<(unsigned)grid, 256, 0, st>>>(a, P);
+      return check_launch("b2k_norm_rope(half)");
+    }
     RowCfg cfg;
     if (!choose_row_cfg(D, Traits<T>::E, 32, &cfg, 4, 256)) {
       set_error("b2k_norm_rope: head dim %lld does not fit", (long long)D);
