@@ -925,6 +925,9 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # stdout carries exactly one JSON line: NCCL's log (its version banner
+        # included) goes to stderr unless the caller chose a log file
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
 
