@@ -16,8 +16,14 @@ Workloads (synthetic data of the named shapes, seeded per rank):
   ce        logits [32768, 128256] bf16, N(0,1)*3, 5% targets = -100,
             mean loss over valid rows (rows split across ranks, NCCL
             all-reduce of [loss sum, valid count])
+  ce_fwd_bwd  same logits: mean loss and its gradient in one pass
 Each rank processes a full configuration (weak scaling) except `ce`, whose
 32768 rows are split across ranks (strong scaling).
+
+Baselines on the same device and inputs: the reference's PyTorch expressions
+in eager mode (`eager`) and under torch.compile (`compile`, the reference
+harness's own baseline; `--compile-mode max-autotune-no-cudagraphs` is its
+strong one); `--compile` adds the compile baseline to the other configs.
 
 --impl reference times the CPU implementation of the same workload (the
 oracle's numpy restatement of ouroboros/specs.py, all host cores) on a bounded
@@ -135,6 +141,11 @@ class Workload:
     def set_rows(self, n):
         setattr(self, self.ROWS_ATTR, int(n))
 
+    def compile_step(self, mode):
+        """The eager reference expressions of the step under torch.compile
+        (the reference harness's own baseline, ouroboros/harness.py:250-290)."""
+        return torch.compile(self.eager_step, mode=mode, dynamic=False)
+
     def setup(self, device, rank, world): ...
     def step(self): ...
     def bytes_per_step(self) -> int: ...
@@ -247,8 +258,21 @@ class RMSNorm(Workload):
     def eager_step(self):
         x = self.xs[self.i % self.SETS]
         self.i += 1
+        return self._expr(x, self.w)
+
+    @staticmethod
+    def _expr(x, w):
         xf = x.float()  # ouroboros/specs.py:75-78
-        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype) * self.w
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype) * w
+
+    def compile_step(self, mode):
+        fn = torch.compile(self._expr, mode=mode, dynamic=False)
+
+        def st():
+            x = self.xs[self.i % self.SETS]
+            self.i += 1
+            return fn(x, self.w)
+        return st
 
     def config(self):
         return {"workload": "rmsnorm", "M": self.M, "N": self.N, "eps": 1e-6,
@@ -438,6 +462,9 @@ class CrossEntropyFwdBwd(CrossEntropy):
     def bytes_per_step(self):
         rows = self.r1 - self.r0
         return 2 * rows * self.V * 2 + rows * 8  # logits read once, gradient written once
+
+    def compile_step(self, mode):
+        return None  # the step runs autograd's backward: no single compiled graph
 
     def eager_step(self):
         xf = self.x.float().requires_grad_(True)
@@ -879,6 +906,33 @@ def measure_eager(wl, stream, steps=5):
         return None
 
 
+def measure_compile(wl, stream, mode, steps=5, graph_steps=0):
+    """ms per step of the reference expressions under torch.compile, or a
+    one-line reason when that baseline cannot be had.  graph_steps > 0 times
+    it from a CUDA graph, as the workload's own kernel is timed."""
+    try:
+        st = wl.compile_step(mode)
+        if st is None:
+            return None, "not compiled: the step runs autograd"
+        for _ in range(3):  # compiles on the first call
+            st()
+        torch.cuda.synchronize()
+        if graph_steps > 0:
+            try:
+                ms, _ = time_steps(st, max(steps, 2 * graph_steps), stream, graph_steps)
+                return ms, None
+            except Exception:
+                torch.cuda.synchronize()
+        ms, _ = time_steps(st, steps, stream)
+        return ms, None
+    except torch.cuda.OutOfMemoryError:
+        torch.cuda.empty_cache()
+        return None, "out of memory"
+    except Exception as e:  # a compiler failure is reported, not fatal
+        torch.cuda.synchronize()
+        return None, f"{type(e).__name__}: {str(e)[:120]}"
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -892,6 +946,13 @@ def main():
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the device-only measurement of the other configurations")
     ap.add_argument("--no-eager", action="store_true")
+    ap.add_argument("--no-compile", action="store_true",
+                    help="skip the torch.compile baseline of the headline workload")
+    ap.add_argument("--compile", action="store_true",
+                    help="also time the torch.compile baseline of the other configurations")
+    ap.add_argument("--compile-mode", default="default",
+                    help="torch.compile mode of the baseline (the reference harness's strong "
+                         "baseline is max-autotune-no-cudagraphs)")
     ap.add_argument("--graph", type=int, default=1,
                     help="launch small workloads from a CUDA graph (1) or one by one (0)")
     ap.add_argument("--grid", default="",
@@ -955,6 +1016,15 @@ def main():
         if e_ms is not None:
             eager = {"ms_per_step": round(e_ms, 4), "speedup": round(e_ms / ms, 2),
                      "what": "the reference's PyTorch expressions (ouroboros/specs.py), eager"}
+    compiled = None
+    if not args.no_compile:
+        c_ms, why = measure_compile(wl, stream, args.compile_mode,
+                                    graph_steps=wl.graph_steps if args.graph else 0)
+        compiled = ({"ms_per_step": round(c_ms, 4), "speedup": round(c_ms / ms, 2)} if c_ms
+                    else {"unavailable": why})
+        compiled.update({"mode": args.compile_mode,
+                         "what": "the same expressions under torch.compile (the reference "
+                                 "harness's baseline)"})
 
     # end to end through the host-buffer API (pinned host in, pinned host out)
     e2e = None
@@ -1025,6 +1095,14 @@ def main():
                 if e2 is not None:
                     entry["eager_ms_per_step"] = round(e2, 4)
                     entry["speedup_vs_eager"] = round(e2 / m2_local, 2)
+            if args.compile:
+                c2, why = measure_compile(w2, stream, args.compile_mode, 3,
+                                          w2.graph_steps if args.graph else 0)
+                if c2:
+                    entry["compile_ms_per_step"] = round(c2, 4)
+                    entry["speedup_vs_compile"] = round(c2 / m2_local, 2)
+                else:
+                    entry["compile_unavailable"] = why
             extra[w2.name] = entry
             del w2
             torch.cuda.empty_cache()
@@ -1045,6 +1123,7 @@ def main():
         "e2e": e2e,
         "cpu_baseline": cpu,
         "eager": eager,
+        "compile": compiled,
         "gpu_launches": launches,
         "clocks": clocks,
         "other_configs": extra or None,
