@@ -56,15 +56,42 @@ __global__ void __launch_bounds__(1024) ce_rows_kernel(const CeArgs a) {
   const bool bad = !ignore && (t < 0 || t >= N);
   const T* xr = static_cast<const T*>(a.x) + (valid ? row * a.ldx : 0);
 
+  // the target logit, loaded now so that its latency overlaps the row
+  const float xt = (valid && !ignore && !bad && g.tx == 0) ? to_f<T>(xr[t]) : 0.0f;
   float m = -INFINITY, s = 0.0f;
   if (valid && !ignore && !bad) {
     const int64_t step = (int64_t)g.G * E;
     for (int64_t c0 = (int64_t)g.tx * E; c0 < N; c0 += step * kCeU) {
       float2 v[kCeU][H];
+      if (a.aligned && c0 + (kCeU - 1) * step + E <= N) {  // whole group: no bounds checks
 #pragma unroll
-      for (int u = 0; u < kCeU; ++u)
-        load_vec_fill<T, true>(reinterpret_cast<float*>(v[u]), xr, c0 + u * step, N, a.aligned,
-                               -INFINITY);
+        for (int u = 0; u < kCeU; ++u) unpack2<T>(ld_stream(xr + c0 + u * step), v[u]);
+      } else {
+#pragma unroll
+        for (int u = 0; u < kCeU; ++u)
+          load_vec_fill<T, true>(reinterpret_cast<float*>(v[u]), xr, c0 + u * step, N,
+                                 a.aligned, -INFINITY);
+      }
+      if constexpr (!P) {
+        // lazy rescale, as in ce_tma_kernel: keep the running maximum while
+        // the group's partial sum against it stays below 2^64
+        if (m != -INFINITY) {
+          const float2 nz = f2s(-m * kLog2e);
+          float2 acc = f2s(0.0f);
+#pragma unroll
+          for (int u = 0; u < kCeU; ++u)
+#pragma unroll
+            for (int j = 0; j < H; ++j) {
+              const float2 z = fma2(v[u][j], f2s(kLog2e), nz);
+              acc = add2(acc, f2(ex2_approx(z.x), ex2_approx(z.y)));
+            }
+          const float part = acc.x + acc.y;
+          if (part < 0x1p64f) {
+            s += part;
+            continue;
+          }
+        }
+      }
       float bm = -INFINITY;
 #pragma unroll
       for (int u = 0; u < kCeU; ++u)
@@ -99,7 +126,7 @@ __global__ void __launch_bounds__(1024) ce_rows_kernel(const CeArgs a) {
     float loss;
     if (ignore) loss = 0.0f;
     else if (bad) loss = __int_as_float(0x7fc00000);  // NaN: target outside [0, N)
-    else loss = (m + (P ? logf(s) : f_log<false>(s))) - to_f<T>(xr[t]);
+    else loss = (m + (P ? logf(s) : f_log<false>(s))) - xt;
     static_cast<OutT*>(a.loss)[row] = from_f<OutT>(loss);
   }
 }
