@@ -769,9 +769,12 @@ def run_grid(args, device):
     for op in ops:
         kind = regimes.OPS[op].kind
         cells = ROPE_GRID if kind in ("rope", "rope_inter", "qkr", "arr") else MATRIX_GRID
+        if args.cells:
+            want = {tuple(int(v) for v in c.split("x")) for c in args.cells.split(",")}
+            cells = [c for c in cells if c in want] or sorted(want)
         res = []
         for (M, N) in cells:
-            for dname in ("fp16", "bf16"):
+            for dname in [d for d in ("fp16", "bf16") if d in args.dtypes.split(",")]:
                 inp = _grid_inputs(kind, M, N, tdt[dname], device, 1000 + M + N)
                 run = b200k.get_op(op)
                 out = run(*inp)
@@ -957,6 +960,9 @@ def main():
                     help="launch small workloads from a CUDA graph (1) or one by one (0)")
     ap.add_argument("--grid", default="",
                     help="shape-grid mode: comma list of ops (or 'all'); one JSON line per op")
+    ap.add_argument("--cells", default="",
+                    help="grid mode: only these shapes, comma list of MxN (e.g. 32768x128)")
+    ap.add_argument("--dtypes", default="fp16,bf16", help="grid mode: dtypes to run")
     ap.add_argument("--rows", type=int, default=0,
                     help="override the row count of the workload (M; batch for rope; "
                          "tokens for ce) — small cases for profiler captures")
