@@ -136,7 +136,11 @@ struct RopeQkArgs {
 // on B200: one position per block beats 2 or 4 per block.)
 constexpr int kRopePos = 1;
 
-template <typename T, bool INTER>
+// INTER: 0 half-split (neox), 1 interleaved pairs with the thread's vectors
+// c and c + D/2 (8-byte table loads), 2 interleaved pairs with two adjacent
+// vectors per thread, whose E table entries are one 16-byte load of cos and
+// one of sin (16-byte aligned tables)
+template <typename T, int INTER>
 __global__ void __launch_bounds__(1024) rope_qk_kernel(const RopeQkArgs a) {
   constexpr int E = Traits<T>::E;
   constexpr int HP = E / 2;
@@ -151,7 +155,42 @@ __global__ void __launch_bounds__(1024) rope_qk_kernel(const RopeQkArgs a) {
     const int64_t hoff = (int64_t)(isq ? hh : hh - (int)a.H) * D;
     const T* src = (isq ? static_cast<const T*>(a.q) : static_cast<const T*>(a.k)) + hoff;
     T* dst = (isq ? static_cast<T*>(a.qo) : static_cast<T*>(a.ko)) + hoff;
-    if (!INTER) {
+    if constexpr (INTER == 2) {
+      const int c2 = threadIdx.x * 2 * E;
+      uint4 rx[kRopePos][2], rc[kRopePos], rs[kRopePos];
+#pragma unroll
+      for (int u = 0; u < kRopePos; ++u) {
+        const int64_t p = p0 + u;
+        if (p < npos) {
+          const int64_t s = p % a.S;
+          rx[u][0] = ld_stream(src + p * hstride + c2);
+          rx[u][1] = ld_stream(src + p * hstride + c2 + E);
+          rc[u] = ld_keep(static_cast<const T*>(a.cos) + s * half + c2 / 2);
+          rs[u] = ld_keep(static_cast<const T*>(a.sin) + s * half + c2 / 2);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kRopePos; ++u) {
+        const int64_t p = p0 + u;
+        if (p < npos) {
+          float cs[E], sn[E];
+          unpack<T>(rc[u], cs);
+          unpack<T>(rs[u], sn);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            float xv[E], o[E];
+            unpack<T>(rx[u][h2], xv);
+#pragma unroll
+            for (int i = 0; i < HP; ++i) {
+              const float cc = cs[h2 * HP + i], ss = sn[h2 * HP + i];
+              o[2 * i] = xv[2 * i] * cc - xv[2 * i + 1] * ss;
+              o[2 * i + 1] = xv[2 * i + 1] * cc + xv[2 * i] * ss;
+            }
+            st_stream(dst + p * hstride + c2 + h2 * E, pack<T>(o));
+          }
+        }
+      }
+    } else if constexpr (INTER == 0) {
       uint4 r1[kRopePos], r2[kRopePos], rc[kRopePos], rs[kRopePos];
 #pragma unroll
       for (int u = 0; u < kRopePos; ++u) {
@@ -490,10 +529,17 @@ extern "C" int b2k_rope_qk(const void* q, const void* k, const void* cos, const 
       const dim3 block(per_head, hpp);
       const int64_t grid = (B * S + kRopePos - 1) / kRopePos;
       B2K_REQUIRE(grid <= 0x7fffffffLL, "b2k_rope_qk: too many positions");
-      if (interleaved)
-        rope_qk_kernel<T, true><<<(unsigned)grid, block, 0, st>>>(a);
+      static const int use_adj = [] {
+        const char* s = getenv("B2K_ROPE_ADJ");
+        return s ? atoi(s) : 1;
+      }();
+      const bool adj = use_adj && aligned16(cos) && aligned16(sin) && ((D / 2) * es) % 16 == 0;
+      if (interleaved && adj)
+        rope_qk_kernel<T, 2><<<(unsigned)grid, block, 0, st>>>(a);
+      else if (interleaved)
+        rope_qk_kernel<T, 1><<<(unsigned)grid, block, 0, st>>>(a);
       else
-        rope_qk_kernel<T, false><<<(unsigned)grid, block, 0, st>>>(a);
+        rope_qk_kernel<T, 0><<<(unsigned)grid, block, 0, st>>>(a);
     } else {
       const int64_t items = B * S * (H + Hk) * (D / 2);
       if (interleaved)
