@@ -212,3 +212,52 @@ def test_cross_entropy_nonfinite_logits_give_nan(dt):
     assert abs(float(loss[5]) - float(np.log(V))) < 2e-2 * float(np.log(V))
     _, g = b200k.cross_entropy_fwd_bwd(x, tgt)
     assert torch.isnan(g[0].float()).any() and torch.isfinite(g[5].float()).all()
+
+
+# ------------------------------------------------- fallback kernel mappings
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("D", [96, 128])
+def test_qknorm_rope_general_kernel(dt, D):
+    """qknorm_rope / add_rmsnorm_rope through the general shared-memory kernel:
+    rows with a stride of D + 1 elements (never 16-byte aligned), starting at
+    element 0 or 1, and D = 96 (half a row is not a power-of-two number of
+    vectors).  Contiguous power-of-two head dims (the per-lane both-halves
+    kernel) are covered by the parity cases."""
+    M = 77
+    x = _randn((M, D + 1), dt, 3.0, 41)
+    r = _randn((M, D + 1), dt, 3.0, 42)
+    w = _randn((D,), dt, 1.0, 43)
+    c = _randn((M, D), dt, 1.0, 44)
+    s = _randn((M, D), dt, 1.0, 45)
+    for off in (0, 1):  # off = 1: misaligned row starts
+        xv, rv = x[:, off:off + D], r[:, off:off + D]
+        got = b200k.qknorm_rope(_t(x, dt)[:, off:off + D], _t(w, dt), _t(c, dt), _t(s, dt))
+        _close(got, O.qknorm_rope(xv, w, c, s, dt), dt, "qknorm_rope")
+        got = b200k.add_rmsnorm_rope(_t(x, dt)[:, off:off + D], _t(r, dt)[:, off:off + D],
+                                     _t(w, dt), _t(c, dt), _t(s, dt))
+        _close(got, O.add_rmsnorm_rope(xv, rv, w, c, s, dt), dt, "add_rmsnorm_rope")
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_rope_qk_interleaved_8byte_tables(dt):
+    """Interleaved q/k RoPE whose tables are 8- but not 16-byte aligned (a view
+    offset by 4 entries) takes the split-vector mapping with 8-byte table
+    loads; aligned tables take the adjacent-vector mapping.  Both against the
+    oracle."""
+    B, S, H, Hk, D = 2, 17, 3, 1, 128
+    q = _randn((B, S, H, D), dt, 4.0, 51)
+    k = _randn((B, S, Hk, D), dt, 4.0, 52)
+    ang = np.arange(S, dtype=np.float32)[:, None] * (
+        10000.0 ** (-np.arange(0, D, 2, dtype=np.float32) / D))[None, :]
+    c, s = rnd(np.cos(ang), dt), rnd(np.sin(ang), dt)
+    def shifted(a):  # contiguous, storage starting 4 entries (8 bytes) into a buffer
+        flat = _t(np.concatenate([np.zeros(4, np.float32), a.ravel()]), dt)
+        return flat[4:].view(a.shape)
+
+    rq, rk = O.rope_qk_tables(q, k, c, s, dt, interleaved=True)
+    for ct, st in ((_t(c, dt), _t(s, dt)), (shifted(c), shifted(s))):
+        assert ct.is_contiguous()
+        qo, ko = b200k.rope_qk(_t(q, dt), _t(k, dt), ct, st, interleaved=True)
+        torch.cuda.synchronize()
+        _close(qo, rq, dt)
+        _close(ko, rk, dt)
