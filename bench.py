@@ -363,7 +363,7 @@ class CrossEntropy(Workload):
     NCCL all-reduce of [loss sum, valid count] inside every step."""
     name = "cross_entropy_mean"
     scaling = "strong"
-    launches_per_step = 3  # row losses, shard reduce, mean
+    launches_per_step = 3  # row losses, shard reduce, mean (2 with the peer exchange)
     T, V = 32768, 128256
     ROWS_ATTR = "T"
 
@@ -382,6 +382,12 @@ class CrossEntropy(Workload):
         self.t = torch.where(drop, torch.full_like(t, -100), t)
         self.world = world
         self.device = device
+        if world > 1 and type(self) is CrossEntropy:
+            # collective set-up of the peer-memory exchange (every rank, same order):
+            # row losses + fused reduce / exchange / mean = 2 launches per step
+            from b200k.dist import ce_exchange
+            if ce_exchange(None, device) is not None:
+                self.launches_per_step = 2
 
     def _chunked(self, rows, device, g):
         out = torch.empty((rows, self.V), dtype=torch.bfloat16, device=device)
@@ -662,7 +668,7 @@ def run_mlp_block(args, device):
             "speedup_vs_eager": round(te / to, 4),
             "nongemm_ms": {"eager": round(tne, 4), "b200k": round(tno, 4)},
             "amdahl_bound_vs_eager": round(1.0 / (1.0 - (tne - tno) / te), 4)}
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0 if ok else 1
 
 
@@ -806,10 +812,9 @@ def run_grid(args, device):
                 del inp, out
         sp = [c["speedup_vs_eager"] for c in res if "speedup_vs_eager" in c]
         geo = float(np.exp(np.mean(np.log(sp)))) if sp else None
-        print(json.dumps({"op": op, "cells": res, "all_parity": all(c["parity"] for c in res),
-                          "geomean_speedup_vs_eager": round(geo, 3) if geo else None,
-                          "mean_frac": round(float(np.mean([c["frac"] for c in res])), 3)}),
-              flush=True)
+        emit({"op": op, "cells": res, "all_parity": all(c["parity"] for c in res),
+              "geomean_speedup_vs_eager": round(geo, 3) if geo else None,
+              "mean_frac": round(float(np.mean([c["frac"] for c in res])), 3)})
     return 0
 
 
@@ -909,6 +914,27 @@ def measure_eager(wl, stream, steps=5):
         return None
 
 
+_OUT = None
+
+
+def _json_out():
+    """The stream the JSON lines go to: the process's original stdout.  On
+    first use file descriptor 1 is pointed at stderr, so that whatever a
+    library prints (NCCL's version banner, compiler logs) cannot land beside
+    the JSON line."""
+    global _OUT
+    if _OUT is None:
+        sys.stdout.flush()
+        fd = os.dup(1)
+        os.dup2(2, 1)
+        _OUT = os.fdopen(fd, "w")
+    return _OUT
+
+
+def emit(obj):
+    print(json.dumps(obj), file=_json_out(), flush=True)
+
+
 def measure_compile(wl, stream, mode, steps=5, graph_steps=0):
     """ms per step of the reference expressions under torch.compile, or a
     one-line reason when that baseline cannot be had.  graph_steps > 0 times
@@ -937,6 +963,7 @@ def measure_compile(wl, stream, mode, steps=5, graph_steps=0):
 
 
 def main():
+    _json_out()  # from here on, fd 1 is stderr; the JSON lines keep the real stdout
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -992,9 +1019,6 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        # stdout carries exactly one JSON line: NCCL's log (its version banner
-        # included) goes to stderr unless the caller chose a log file
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
 
@@ -1135,9 +1159,12 @@ def main():
         "other_configs": extra or None,
     }
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist is not None:
+        torch.cuda.synchronize()
         dist.barrier()
+        from b200k.dist import close_exchanges
+        close_exchanges()  # peer mappings of the cross-entropy exchange
         dist.destroy_process_group()
 
 
@@ -1177,7 +1204,7 @@ def run_reference(args, wl, rank, world):
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 if __name__ == "__main__":

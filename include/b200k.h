@@ -196,6 +196,40 @@ int b2k_ce_mean(const double* sumcount, float* out, void* stream);
 int b2k_ce_valid_count(const int64_t* tgt, int64_t M, int64_t ignore_index,
                        double* count, void* stream);
 
+/* Bytes of one rank's exchange buffer for b2k_ce_reduce_exchange_mean with
+ * `world` ranks (1..32; -1 otherwise). */
+int64_t b2k_ce_exchange_bytes(int world);
+
+/* b2k_ce_reduce, the all-reduce of its [sum, count] pair across `world` ranks
+ * and b2k_ce_mean in ONE kernel, the exchange over peer memory instead of a
+ * collective library: peers is a DEVICE array of `world` pointers, peers[r]
+ * = rank r's exchange buffer as mapped in this process (b2k_ce_exchange_alloc
+ * on each rank, mapped with b2k_ipc_handle / b2k_ipc_open; zeroed before the
+ * first call).  Every rank calls it once per step, in the same order.  The block
+ * stores this rank's pair into every rank's buffer, publishes it with a
+ * system-scope release, waits until all ranks' pairs are in its own buffer
+ * (at most limit_ns of global time), and adds them in rank order (the same
+ * bits on every rank).  On success *status = 0, sumcount = global [sum,
+ * count], out[0] = sum / count; on a timeout *status = 1 and out[0] = NaN.
+ * Replaces ouroboros/specs.py's per-row cross-entropy (:239-241) reduced to
+ * the mean over valid rows with the rows sharded across GPUs; the reference
+ * has no multi-GPU path. */
+int b2k_ce_reduce_exchange_mean(const float* row_loss, const int64_t* tgt, int64_t M,
+                                int64_t ignore_index, void* const* peers, int rank, int world,
+                                unsigned long long limit_ns, double* sumcount, float* out,
+                                int* status, void* stream);
+
+/* Exchange-buffer plumbing (no reference counterpart): a zeroed device
+ * allocation of b2k_ce_exchange_bytes(world) bytes on the current device, its
+ * 64-byte CUDA IPC handle, and the mapping of a peer process's buffer from
+ * its handle (plain peer access; no multicast object), each with its
+ * release. */
+int b2k_ce_exchange_alloc(int world, void** buf);
+int b2k_ce_exchange_free(void* buf);
+int b2k_ipc_handle(void* buf, void* handle64);
+int b2k_ipc_open(const void* handle64, void** ptr);
+int b2k_ipc_close(void* ptr);
+
 /* Forward and backward of the reduced cross-entropy in one kernel: per-row
  * fp32 losses as b2k_cross_entropy, and the gradient of
  * grad_scale * mean-over-valid-rows(loss) w.r.t. the logits,

@@ -54,6 +54,15 @@ SIGNATURES = {
                                   c_int, c_int64, c_void_p]),
     "b2k_ce_reduce": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
     "b2k_ce_mean": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "b2k_ce_exchange_bytes": (c_int64, [c_int]),
+    "b2k_ce_exchange_alloc": (c_int, [c_int, c_void_p]),
+    "b2k_ce_exchange_free": (c_int, [c_void_p]),
+    "b2k_ipc_handle": (c_int, [c_void_p, c_void_p]),
+    "b2k_ipc_open": (c_int, [c_void_p, c_void_p]),
+    "b2k_ipc_close": (c_int, [c_void_p]),
+    "b2k_ce_reduce_exchange_mean": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int,
+                                            c_int, ctypes.c_ulonglong, c_void_p, c_void_p,
+                                            c_void_p, c_void_p]),
     "b2k_ce_valid_count": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
     "b2k_cross_entropy_fwd_bwd": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int,
                                           c_int64, c_void_p, c_float, c_void_p, c_void_p,

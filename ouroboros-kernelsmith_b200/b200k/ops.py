@@ -523,7 +523,7 @@ def cross_entropy_mean(logits, tgt, ignore_index: int = -100, group=None):
     (one NCCL all-reduce of [loss sum, valid count]).  Per-row losses are the
     spec op's (specs.py:239-241) in fp32; their sum is accumulated in fp64 in
     a fixed order."""
-    from .dist import allreduce_sumcount
+    from .dist import XCHG_LIMIT_NS, allreduce_sumcount, ce_exchange
     dev = _cuda(logits, tgt)
     dt = _dtype_id(logits)
     n = logits.shape[-1]
@@ -533,10 +533,18 @@ def cross_entropy_mean(logits, tgt, ignore_index: int = -100, group=None):
     row_loss = torch.empty((m,), dtype=torch.float32, device=dev)
     sumcount = torch.empty((2,), dtype=torch.float64, device=dev)
     out = torch.empty((), dtype=torch.float32, device=dev)
+    xchg = ce_exchange(group, dev)
     with _dev(dev) as stream:
         st = L.lib.b2k_cross_entropy(_p(x2), ldx, _p(t1), _p(row_loss), m, n, dt, L.F32,
                                      ignore_index, stream)
         L.check(st, "b2k_cross_entropy")
+        if xchg is not None:
+            # reduce + exchange over peer memory + mean, one kernel
+            L.check(L.lib.b2k_ce_reduce_exchange_mean(
+                _p(row_loss), _p(t1), m, ignore_index, _p(xchg.peers), xchg.rank, xchg.world,
+                XCHG_LIMIT_NS, _p(sumcount), _p(out), _p(xchg.status), stream),
+                "b2k_ce_reduce_exchange_mean")
+            return out
         L.check(L.lib.b2k_ce_reduce(_p(row_loss), _p(t1), m, ignore_index, _p(sumcount), stream),
                 "b2k_ce_reduce")
     allreduce_sumcount(sumcount, group)
