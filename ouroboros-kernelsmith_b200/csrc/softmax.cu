@@ -284,7 +284,8 @@ static int softmax_launch(const SoftmaxArgs& a, cudaStream_t st) {
       auto kern = vneed <= 2 ? softmax_tma_kernel<T, KIND, 2> : softmax_tma_kernel<T, KIND, 4>;
       static const int want_cps = env_int("B2K_TMA_CPS", 0);
       static const int want_st = env_int("B2K_TMA_STAGES", 0);
-      if (choose_pipe_shape(kern, G, row_bytes, want_cps, want_st, &ps)) {
+      // 2-stage ring unless set: measured equal or faster on the spec grid
+      if (choose_pipe_shape(kern, G, row_bytes, want_cps, want_st > 0 ? want_st : 2, &ps)) {
         const size_t smem = RowPipe<1>::smem_bytes(ps.S, row_bytes);
         int64_t grid = (int64_t)sm_count() * ps.cps;
         if (grid > a.M) grid = a.M;
