@@ -6,7 +6,7 @@ One JSON line on stdout (rank 0).  Metric: achieved HBM GB/s of the op
 (algorithmic bytes: compulsory reads + writes, per step) aggregated over all
 ranks, with the % of the measured HBM peak in `roofline`.
 
-Workloads (synthetic data of the named shapes, seeded per rank):
+Workloads (synthetic data of the named shapes):
   chain     (default) residual add -> LayerNorm -> GELU-tanh, bf16,
             x, r [16384, 8192], outputs (h = x + r, y), eps 1e-5
   rmsnorm   x [4096, 4096] fp16, w = 1 + 0.1 N(0,1), eps 1e-6
@@ -14,16 +14,28 @@ Workloads (synthetic data of the named shapes, seeded per rank):
   rope      q [8,4096,32,128], k [8,4096,8,128] bf16, tables [4096, 64] (neox)
   rope_interleaved   same shapes, GPT-J pairs
   ce        logits [32768, 128256] bf16, N(0,1)*3, 5% targets = -100,
-            mean loss over valid rows (rows split across ranks, NCCL
-            all-reduce of [loss sum, valid count])
+            mean loss over valid rows (one exchange of [loss sum, valid
+            count] between the ranks inside every step)
   ce_fwd_bwd  same logits: mean loss and its gradient in one pass
-Each rank processes a full configuration (weak scaling) except `ce`, whose
-32768 rows are split across ranks (strong scaling).
+Every workload is one fixed problem whose rows are split across the ranks
+(strong scaling): rank r of N owns the contiguous rows shard_rows(M, r, N)
+(the batch for rope, the tokens for ce).
 
-Baselines on the same device and inputs: the reference's PyTorch expressions
-in eager mode (`eager`) and under torch.compile (`compile`, the reference
-harness's own baseline; `--compile-mode max-autotune-no-cudagraphs` is its
-strong one); `--compile` adds the compile baseline to the other configs.
+Timing: W warm-up steps, then exactly K steps captured in one CUDA graph and
+replayed between CUDA events on the launching stream (the graph removes the
+host's launch gaps, which dominate the microsecond shards of the small
+configurations; `--graph 0` launches step by step).  Each rank holds enough
+input sets, used in rotation, that a step's inputs were last touched at least
+3 x L2 of traffic earlier, so every step reads from HBM.  The reported time
+is the maximum over ranks; the per-rank spread is printed beside it.  After
+the timed region the last timed output is checked against the reference's
+PyTorch expression on the same inputs (`parity`), as ouroboros/harness.py
+does after its timing loop.
+
+Baselines on the same device and inputs (N = 1): the reference's PyTorch
+expressions in eager mode, under torch.compile (default mode, the reference
+harness's baseline) and under torch.compile max-autotune-no-cudagraphs (its
+strong baseline, ouroboros/harness.py:282-287).
 
 --impl reference times the CPU implementation of the same workload (the
 oracle's numpy restatement of ouroboros/specs.py, all host cores) on a bounded
@@ -32,7 +44,9 @@ sample of rows per step, on rank 0 only.
 from __future__ import annotations
 
 import argparse
+import collections
 import json
+import math
 import os
 import statistics
 import sys
@@ -46,7 +60,12 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 L2_BYTES = 126 * 1024 * 1024
+ROTATE_BYTES = 3 * L2_BYTES  # per-rank traffic between two uses of one input set
 FALLBACK_HBM_GBS = 6650.0
+# the spec's allclose tolerance per output dtype: the element-wise minimum of
+# ouroboros/specs.py:41-45 and fp16 1e-2 / bf16 2e-2 (rtol, atol)
+TOL = {torch.float16: (1e-2, 2e-3), torch.bfloat16: (2e-2, 8e-3), torch.float32: (2e-4, 2e-5)}
+CE_MEAN_RTOL = 1e-3  # relative tolerance of the reduced cross-entropy scalar
 
 
 # ---------------------------------------------------------------------------
@@ -121,85 +140,164 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # workloads
 def _randn(shape, dtype, device, seed, scale=1.0, shift=0.0):
+    """N(0,1)*scale+shift in `dtype`, generated in row blocks of at most 2^30
+    elements (keeps the fp32 temporary small for the 8 GB logits)."""
     g = torch.Generator(device=device).manual_seed(seed)
-    return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * scale
-            + shift).to(dtype)
+    out = torch.empty(shape, dtype=dtype, device=device)
+    flat = out.view(shape[0], -1) if len(shape) > 1 else out.view(-1, 1)
+    step = max(1, (1 << 30) // max(1, flat.shape[1]))
+    for r in range(0, flat.shape[0], step):
+        n = min(step, flat.shape[0] - r)
+        flat[r:r + n] = (torch.randn((n, flat.shape[1]), generator=g, device=device,
+                                     dtype=torch.float32) * scale + shift).to(dtype)
+    return out
+
+
+def _close(got, want, dtype):
+    """(ok, max abs error) of |got - want| <= atol + rtol |want|, element-wise,
+    at the spec tolerance of `dtype`, computed in fp32 on the device."""
+    rtol, atol = TOL[dtype]
+    g, w = got.float(), want.float()
+    err = (g - w).abs()
+    ok = bool((err <= atol + rtol * w.abs()).all()) and bool(torch.isfinite(g).all())
+    return ok, float(err.max()) if err.numel() else 0.0
 
 
 class Workload:
+    """One named configuration, row-sharded over the ranks.
+
+    Subclasses define the row count (attribute ROWS_ATTR), `make_set(k)` (the
+    k-th input set of this rank's shard), `run(*inputs)` (the b200k call),
+    `expr(*inputs)` (the reference's PyTorch expression of the same outputs,
+    used for the eager / compile baselines and the parity check) and
+    `bytes_per_step()` (algorithmic bytes of this rank's shard)."""
     name = ""
-    scaling = "weak"
+    scaling = "strong"
     dtype = "bf16"
     launches_per_step = 1
-    graph_steps = 0  # > 0: time from a CUDA graph of this many steps (launch-bound sizes)
-
-    def e2e_api(self):
-        return "b200k.host.run_rows_host (pinned host buffers, copies overlapped with kernels)"
-
     ROWS_ATTR = "M"
+    graphable = True  # the step can be captured in a CUDA graph
+
+    def rows_total(self):
+        return int(getattr(self, self.ROWS_ATTR))
 
     def set_rows(self, n):
         setattr(self, self.ROWS_ATTR, int(n))
 
-    def compile_step(self, mode):
-        """The eager reference expressions of the step under torch.compile
-        (the reference harness's own baseline, ouroboros/harness.py:250-290)."""
-        return torch.compile(self.eager_step, mode=mode, dynamic=False)
+    def setup(self, device, rank, world):
+        import b200k
+        from b200k.dist import shard_rows
+        self.b2k = b200k
+        self.device, self.rank, self.world = device, rank, world
+        self.r0, self.r1 = shard_rows(self.rows_total(), rank, world)
+        self.rows = self.r1 - self.r0
+        self.make_shared()
+        per = max(1, self.bytes_per_step())
+        self.nsets = int(max(1, min(64, -(-ROTATE_BYTES // per))))
+        self.sets = [self.make_set(k) for k in range(self.nsets)]
+        self.i = 0
+        self.last_set = 0
 
-    def setup(self, device, rank, world): ...
-    def step(self): ...
-    def bytes_per_step(self) -> int: ...
+    def make_shared(self):
+        """Operands every rank holds in full (weights, tables)."""
+
+    def seed(self, k, j):
+        """Seed of operand j of input set k on this rank."""
+        return 100003 * self.rank + 1009 * k + 17 * j + 1
+
+    def next_set(self):
+        k = self.i % self.nsets
+        self.i += 1
+        self.last_set = k
+        return self.sets[k]
+
+    def step(self):
+        return self.run(*self.next_set())
+
+    def eager_step(self):
+        return self.expr(*self.next_set())
+
+    def compile_step(self, mode):
+        """The reference expressions under torch.compile (the reference
+        harness's own baselines, ouroboros/harness.py:250-290)."""
+        fn = torch.compile(self.expr, mode=mode, dynamic=False)
+        return lambda: fn(*self.next_set())
+
+    def poke(self):
+        """One large in-range value written into the first input of every set
+        before timing (ouroboros/harness.py:229-250): a result cached across
+        calls would miss it and fail the check after the timed region."""
+        for k, s in enumerate(self.sets):
+            flat = s[0].view(-1)
+            flat[(7919 * (k + 1)) % flat.numel()] = 60.0
+
+    def verify(self, out):
+        """Compares the output of the last step with the reference
+        expression on that step's inputs."""
+        want = self.expr(*self.sets[self.last_set])
+        ok, err = _close(out, want, out.dtype)
+        return {"parity": ok, "max_abs_err": err, "checked": "all rows vs the fp32 torch expression"}
+
     def config(self) -> dict: ...
-    def e2e_setup(self): ...
-    def e2e_step(self, timing): ...
-    def cpu_rows(self) -> int: ...
-    def cpu_run(self, r0, r1): ...
+    def bytes_per_step(self) -> int: ...
+    def make_set(self, k): ...
+    def run(self, *inputs): ...
+    def expr(self, *inputs): ...
+
+    def e2e_api(self):
+        return "b200k.host.run_rows_host (pinned host buffers, copies overlapped with kernels)"
 
 
 class Chain(Workload):
-    """x + r -> LayerNorm -> GELU-tanh, outputs (h, y); configs[1] shape."""
+    """x + r -> LayerNorm -> GELU-tanh, outputs (h, y): add_layernorm_gelu of
+    ouroboros/chains.py:69-87 plus the residual stream h, 16384 x 8192 bf16."""
     name = "chain_add_layernorm_gelu"
     M, N = 16384, 8192
 
-    def setup(self, device, rank, world):
-        import b200k
-        self.b2k = b200k
-        s = 1000 * rank
-        self.x = _randn((self.M, self.N), torch.bfloat16, device, s + 1)
-        self.r = _randn((self.M, self.N), torch.bfloat16, device, s + 2)
-        self.w = _randn((self.N,), torch.bfloat16, device, s + 3, 0.1, 1.0)
-        self.b = _randn((self.N,), torch.bfloat16, device, s + 4, 0.02)
-        self.device = device
+    def make_shared(self):
+        self.w = _randn((self.N,), torch.bfloat16, self.device, 3, 0.1, 1.0)
+        self.b = _randn((self.N,), torch.bfloat16, self.device, 4, 0.02)
 
-    def step(self):
-        return self.b2k.fused_add_norm(self.x, self.r, self.w, self.b, norm="layer", act="gelu")
+    def make_set(self, k):
+        return (_randn((self.rows, self.N), torch.bfloat16, self.device, self.seed(k, 1)),
+                _randn((self.rows, self.N), torch.bfloat16, self.device, self.seed(k, 2)))
+
+    def run(self, x, r):
+        return self.b2k.fused_add_norm(x, r, self.w, self.b, norm="layer", act="gelu")
 
     def bytes_per_step(self):
         # read x, r; write h, y (bf16); read gamma, beta
-        return 4 * self.M * self.N * 2 + 2 * self.N * 2
+        return 4 * self.rows * self.N * 2 + 2 * self.N * 2
 
     def config(self):
         return {"workload": "add_layernorm_gelu_tanh_h_y", "M": self.M, "N": self.N,
-                "outputs": "h=x+r, y=gelu_tanh(LN(h)*g+b)", "eps": 1e-5,
-                "l2": "inputs exceed L2 (1 GiB working set per step)"}
+                "outputs": "h=x+r, y=gelu_tanh(LN(h)*g+b)", "eps": 1e-5}
 
-    def eager_step(self):
-        # ouroboros/chains.py:69-87 (add_layernorm_gelu) in torch eager, plus h
-        hf = self.x.float() + self.r.float()
+    def expr(self, x, r):
+        # ouroboros/chains.py:69-87 (add_layernorm_gelu) in torch, plus h
+        hf = x.float() + r.float()
         mu = hf.mean(-1, keepdim=True)
         hc = hf - mu
-        n = hc * torch.rsqrt((hc * hc).mean(-1, keepdim=True) + 1e-5) * self.w.float() + self.b.float()
-        y = (0.5 * n * (1.0 + torch.tanh(0.7978845608028654 * (n + 0.044715 * n * n * n))))
+        n = hc * torch.rsqrt((hc * hc).mean(-1, keepdim=True) + 1e-5) * self.w.float() \
+            + self.b.float()
+        y = 0.5 * n * (1.0 + torch.tanh(0.7978845608028654 * (n + 0.044715 * n * n * n)))
         return hf.to(torch.bfloat16), y.to(torch.bfloat16)
 
+    def verify(self, out):
+        h, y = out
+        h_want, y_want = self.expr(*self.sets[self.last_set])
+        ok_y, err = _close(y, y_want, torch.bfloat16)
+        ok_h = bool(torch.equal(h, h_want))
+        return {"parity": ok_y and ok_h, "max_abs_err": err, "h_bit_exact": ok_h,
+                "checked": "all rows: h bit-exact, y vs the fp32 torch expression"}
+
     def e2e_setup(self):
-        self.hx = self.x.cpu().pin_memory()
-        self.hr = self.r.cpu().pin_memory()
-        self.hw = self.w.cpu()
-        self.hb = self.b.cpu()
+        x, r = self.sets[0]
+        self.hx, self.hr = x.cpu().pin_memory(), r.cpu().pin_memory()
+        self.hw, self.hb = self.w.cpu(), self.b.cpu()
         self.hh = torch.empty_like(self.hx).pin_memory()
         self.hy = torch.empty_like(self.hx).pin_memory()
-        return (2 * self.M * self.N * 2 + 2 * self.N * 2, 2 * self.M * self.N * 2)
+        return (2 * self.rows * self.N * 2 + 2 * self.N * 2, 2 * self.rows * self.N * 2)
 
     def e2e_step(self, timing):
         from b200k.host import run_rows_host
@@ -231,59 +329,36 @@ class Chain(Workload):
 
 
 class RMSNorm(Workload):
-    """rmsnorm x [4096, 4096] fp16; buffers rotate over 8 sets."""
+    """rmsnorm x [4096, 4096] fp16, w = 1 + 0.1 N(0,1), eps 1e-6
+    (ouroboros/specs.py:75-78)."""
     name = "rmsnorm"
     dtype = "fp16"
     M = N = 4096
-    SETS = 8
-    graph_steps = 8
 
-    def setup(self, device, rank, world):
-        import b200k
-        self.b2k = b200k
-        s = 1000 * rank
-        self.xs = [_randn((self.M, self.N), torch.float16, device, s + 10 + i) for i in range(self.SETS)]
-        self.w = _randn((self.N,), torch.float16, device, s + 3, 0.1, 1.0)
-        self.i = 0
-        self.device = device
+    def make_shared(self):
+        self.w = _randn((self.N,), torch.float16, self.device, 3, 0.1, 1.0)
 
-    def step(self):
-        x = self.xs[self.i % self.SETS]
-        self.i += 1
+    def make_set(self, k):
+        return (_randn((self.rows, self.N), torch.float16, self.device, self.seed(k, 1)),)
+
+    def run(self, x):
         return self.b2k.rmsnorm(x, self.w)
 
     def bytes_per_step(self):
-        return 2 * self.M * self.N * 2 + self.N * 2
+        return 2 * self.rows * self.N * 2 + self.N * 2
 
-    def eager_step(self):
-        x = self.xs[self.i % self.SETS]
-        self.i += 1
-        return self._expr(x, self.w)
-
-    @staticmethod
-    def _expr(x, w):
+    def expr(self, x):
         xf = x.float()  # ouroboros/specs.py:75-78
-        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype) * w
-
-    def compile_step(self, mode):
-        fn = torch.compile(self._expr, mode=mode, dynamic=False)
-
-        def st():
-            x = self.xs[self.i % self.SETS]
-            self.i += 1
-            return fn(x, self.w)
-        return st
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype) * self.w
 
     def config(self):
-        return {"workload": "rmsnorm", "M": self.M, "N": self.N, "eps": 1e-6,
-                "l2": f"{self.SETS} rotating input sets ({self.SETS * self.M * self.N * 2 >> 20} MiB) "
-                      "so consecutive steps read cold data"}
+        return {"workload": "rmsnorm", "M": self.M, "N": self.N, "eps": 1e-6}
 
     def e2e_setup(self):
-        self.hx = self.xs[0].cpu().pin_memory()
+        self.hx = self.sets[0][0].cpu().pin_memory()
         self.hw = self.w.cpu()
         self.hy = torch.empty_like(self.hx).pin_memory()
-        return (self.M * self.N * 2 + self.N * 2, self.M * self.N * 2)
+        return (self.rows * self.N * 2 + self.N * 2, self.rows * self.N * 2)
 
     def e2e_step(self, timing):
         from b200k.host import run_rows_host
@@ -306,36 +381,32 @@ class RMSNorm(Workload):
 
 
 class SwiGLU(Workload):
-    """configs[2]: silu(gate) * up, gate/up [8192, 14336] bf16, N(0,1)*2."""
+    """silu(gate) * up, gate/up [8192, 14336] bf16, N(0,1)*2
+    (ouroboros/specs.py:85-87)."""
     name = "swiglu"
     M, N = 8192, 14336
 
-    def setup(self, device, rank, world):
-        import b200k
-        self.b2k = b200k
-        s = 1000 * rank
-        self.g = _randn((self.M, self.N), torch.bfloat16, device, s + 21, 2.0)
-        self.u = _randn((self.M, self.N), torch.bfloat16, device, s + 22, 2.0)
-        self.device = device
+    def make_set(self, k):
+        return (_randn((self.rows, self.N), torch.bfloat16, self.device, self.seed(k, 1), 2.0),
+                _randn((self.rows, self.N), torch.bfloat16, self.device, self.seed(k, 2), 2.0))
 
-    def step(self):
-        return self.b2k.swiglu(self.g, self.u)
+    def run(self, g, u):
+        return self.b2k.swiglu(g, u)
 
     def bytes_per_step(self):
-        return 3 * self.M * self.N * 2
+        return 3 * self.rows * self.N * 2
 
-    def eager_step(self):  # ouroboros/specs.py:85-87
-        return (torch.nn.functional.silu(self.g.float()) * self.u.float()).to(self.g.dtype)
+    def expr(self, g, u):  # ouroboros/specs.py:85-87
+        return (torch.nn.functional.silu(g.float()) * u.float()).to(g.dtype)
 
     def config(self):
-        return {"workload": "swiglu", "M": self.M, "N": self.N,
-                "l2": "inputs exceed L2 (470 MB read per step)"}
+        return {"workload": "swiglu", "M": self.M, "N": self.N}
 
     def e2e_setup(self):
-        self.hg = self.g.cpu().pin_memory()
-        self.hu = self.u.cpu().pin_memory()
+        g, u = self.sets[0]
+        self.hg, self.hu = g.cpu().pin_memory(), u.cpu().pin_memory()
         self.hy = torch.empty_like(self.hg).pin_memory()
-        return (2 * self.M * self.N * 2, self.M * self.N * 2)
+        return (2 * self.rows * self.N * 2, self.rows * self.N * 2)
 
     def e2e_step(self, timing):
         from b200k.host import run_rows_host
@@ -358,69 +429,93 @@ class SwiGLU(Workload):
 
 
 class CrossEntropy(Workload):
-    """mean CE over valid tokens, logits [32768, 128256] bf16,
-    N(0,1)*3, 5% targets = -100; rows split across ranks (strong scaling),
-    NCCL all-reduce of [loss sum, valid count] inside every step."""
+    """Mean CE over valid tokens, logits [32768, 128256] bf16, N(0,1)*3, 5%
+    targets = -100 (ouroboros/specs.py:239-241 reduced over the valid rows);
+    the [loss sum, valid count] pair of every rank is exchanged inside every
+    step (peer-memory exchange fused into the reducing kernel, or an NCCL
+    all-reduce)."""
     name = "cross_entropy_mean"
-    scaling = "strong"
     launches_per_step = 3  # row losses, shard reduce, mean (2 with the peer exchange)
     T, V = 32768, 128256
     ROWS_ATTR = "T"
 
     def setup(self, device, rank, world):
-        import b200k
-        from b200k.dist import shard_rows
-        self.b2k = b200k
-        self.r0, self.r1 = shard_rows(self.T, rank, world)
-        rows = self.r1 - self.r0
-        g = torch.Generator(device=device).manual_seed(500 + rank)
-        self.x = (torch.randn((rows, self.V), generator=g, device=device, dtype=torch.float32)
-                  * 3.0).to(torch.bfloat16) if rows * self.V < (1 << 31) else self._chunked(
-                      rows, device, g)
-        t = torch.randint(0, self.V, (rows,), generator=g, device=device, dtype=torch.int64)
-        drop = torch.rand((rows,), generator=g, device=device) < 0.05
-        self.t = torch.where(drop, torch.full_like(t, -100), t)
-        self.world = world
-        self.device = device
+        super().setup(device, rank, world)
+        self.exchange = "none (1 rank)"
         if world > 1 and type(self) is CrossEntropy:
             # collective set-up of the peer-memory exchange (every rank, same order):
             # row losses + fused reduce / exchange / mean = 2 launches per step
             from b200k.dist import ce_exchange
             if ce_exchange(None, device) is not None:
                 self.launches_per_step = 2
+                self.exchange = "peer memory (CUDA IPC over NVLink), fused into the reduce kernel"
+            else:
+                self.exchange = "NCCL all-reduce"
+                self.graphable = False
 
-    def _chunked(self, rows, device, g):
-        out = torch.empty((rows, self.V), dtype=torch.bfloat16, device=device)
-        step = 4096
-        for r in range(0, rows, step):
-            n = min(step, rows - r)
-            out[r:r + n] = (torch.randn((n, self.V), generator=g, device=device) * 3.0).to(
-                torch.bfloat16)
-        return out
+    def make_set(self, k):
+        x = _randn((self.rows, self.V), torch.bfloat16, self.device, self.seed(k, 1), 3.0)
+        g = torch.Generator(device=self.device).manual_seed(self.seed(k, 2))
+        t = torch.randint(0, self.V, (self.rows,), generator=g, device=self.device,
+                          dtype=torch.int64)
+        drop = torch.rand((self.rows,), generator=g, device=self.device) < 0.05
+        return (x, torch.where(drop, torch.full_like(t, -100), t))
 
-    def step(self):
-        return self.b2k.cross_entropy_mean(self.x, self.t)
+    def run(self, x, t):
+        return self.b2k.cross_entropy_mean(x, t)
 
     def bytes_per_step(self):
-        rows = self.r1 - self.r0
-        return rows * self.V * 2 + rows * 8
+        return self.rows * self.V * 2 + self.rows * 8
 
-    def eager_step(self):
+    def bytes_needed(self):
+        """Bytes the step has to move: the algorithmic bytes less the logits
+        of rows whose target is ignore_index (their loss is 0 without reading
+        them)."""
+        t = self.sets[0][1]
+        ignored = int((t == -100).sum())
+        return self.bytes_per_step() - ignored * self.V * 2
+
+    def expr(self, x, t):
         # ouroboros/specs.py:239-241 reduced to the mean over valid rows
-        return torch.nn.functional.cross_entropy(self.x.float(), self.t, ignore_index=-100)
+        return torch.nn.functional.cross_entropy(x.float(), t, ignore_index=-100)
+
+    def _ref_mean(self, x, t):
+        """fp64 sum of the fp32 per-row losses and the valid count of this
+        rank's shard (row chunks of F.cross_entropy), summed over the ranks
+        with an NCCL all-reduce that is independent of the path under test."""
+        s = torch.zeros((2,), dtype=torch.float64, device=self.device)
+        step = 2048
+        for r in range(0, x.shape[0], step):
+            xs, ts = x[r:r + step].float(), t[r:r + step]
+            s[0] += torch.nn.functional.cross_entropy(xs, ts, ignore_index=-100,
+                                                      reduction="sum").double()
+            s[1] += (ts != -100).sum().double()
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(s, op=dist.ReduceOp.SUM)
+        return float(s[0] / s[1])
+
+    def verify(self, out):
+        want = self._ref_mean(*self.sets[self.last_set])
+        got = float(out)
+        err = abs(got - want)
+        ok = math.isfinite(got) and err <= CE_MEAN_RTOL * abs(want)
+        return {"parity": ok, "max_abs_err": err, "mean": got, "reference_mean": want,
+                "checked": f"mean over all {self.T} rows of all ranks vs F.cross_entropy in fp32 "
+                           f"(row chunks, NCCL-summed), rtol {CE_MEAN_RTOL}"}
 
     def config(self):
         return {"workload": "cross_entropy_mean", "T": self.T, "V": self.V,
                 "ignore_index": -100, "ignore_frac": 0.05,
-                "l2": "inputs exceed L2 (8.4 GB of logits per step)",
                 "note": "rows whose target is ignore_index are not read (their loss is 0)"}
 
     def e2e_setup(self):
         # host buffers for a bounded slice (the full 8.4 GB does not need to
         # sit in pinned memory): 4096 rows
-        self.e2e_rows = min(4096, self.r1 - self.r0)
-        self.hx = self.x[:self.e2e_rows].cpu().pin_memory()
-        self.ht = self.t[:self.e2e_rows].cpu().pin_memory()
+        x, t = self.sets[0]
+        self.e2e_rows = min(4096, self.rows)
+        self.hx = x[:self.e2e_rows].cpu().pin_memory()
+        self.ht = t[:self.e2e_rows].cpu().pin_memory()
         return (self.e2e_rows * (self.V * 2 + 8), 4)
 
     def e2e_bytes(self):
@@ -457,26 +552,54 @@ class CrossEntropy(Workload):
 
 
 class CrossEntropyFwdBwd(CrossEntropy):
-    """configs[4] with the gradient: mean CE over valid tokens and
-    d loss / d logits (bf16) in one pass over the logits."""
+    """The same logits: mean CE over valid tokens and d loss / d logits (bf16)
+    in one pass over the logits."""
     name = "cross_entropy_fwd_bwd"
     launches_per_step = 4  # valid count, fused fwd+bwd, shard reduce, mean
 
-    def step(self):
-        return self.b2k.cross_entropy_fwd_bwd(self.x, self.t)
+    def setup(self, device, rank, world):
+        super().setup(device, rank, world)
+        # two NCCL all-reduces per step when sharded: launched step by step
+        self.graphable = world == 1
+
+    def run(self, x, t):
+        return self.b2k.cross_entropy_fwd_bwd(x, t)
 
     def bytes_per_step(self):
-        rows = self.r1 - self.r0
-        return 2 * rows * self.V * 2 + rows * 8  # logits read once, gradient written once
+        return 2 * self.rows * self.V * 2 + self.rows * 8  # logits read once, gradient written once
 
     def compile_step(self, mode):
         return None  # the step runs autograd's backward: no single compiled graph
 
-    def eager_step(self):
-        xf = self.x.float().requires_grad_(True)
-        loss = torch.nn.functional.cross_entropy(xf, self.t, ignore_index=-100)
+    def expr(self, x, t):
+        xf = x.float().requires_grad_(True)
+        loss = torch.nn.functional.cross_entropy(xf, t, ignore_index=-100)
         loss.backward()
         return loss.detach(), xf.grad.to(torch.bfloat16)
+
+    def verify(self, out):
+        loss, dx = out
+        x, t = self.sets[self.last_set]
+        want = self._ref_mean(x, t)
+        got = float(loss)
+        ok_l = math.isfinite(got) and abs(got - want) <= CE_MEAN_RTOL * abs(want)
+        # gradient of sampled rows against autograd of the same rows' losses,
+        # scaled by the global valid count
+        n_valid = float((t != -100).sum())
+        if self.world > 1:
+            import torch.distributed as dist
+            c = torch.tensor([n_valid], dtype=torch.float64, device=self.device)
+            dist.all_reduce(c, op=dist.ReduceOp.SUM)
+            n_valid = float(c)
+        rows = torch.arange(0, x.shape[0], max(1, x.shape[0] // 64), device=self.device)
+        xf = x[rows].float().requires_grad_(True)
+        torch.nn.functional.cross_entropy(xf, t[rows], ignore_index=-100,
+                                          reduction="sum").backward()
+        # compared at the scale of p - onehot (the gradient times the valid count)
+        ok_g, err = _close(dx[rows].float() * n_valid, xf.grad, torch.bfloat16)
+        return {"parity": ok_l and ok_g, "max_abs_err": err, "mean": got, "reference_mean": want,
+                "checked": "mean over all rows (rtol 1e-3) and the gradient of 64 sampled rows "
+                           "vs autograd in fp32"}
 
     def config(self):
         c = super().config()
@@ -518,39 +641,40 @@ class CrossEntropyFwdBwd(CrossEntropy):
 
 
 class RoPE(Workload):
-    """q [8,4096,32,128], k [8,4096,8,128] bf16, positions 0..S-1,
-    theta 10000, tables [S, 64] computed in fp32 and cast to bf16; q and k
-    rotated in one launch into fresh outputs."""
+    """q [8,4096,32,128], k [8,4096,8,128] bf16, positions 0..S-1, theta 10000,
+    tables [S, 64] computed in fp32 and cast to bf16; q and k rotated in one
+    launch into fresh outputs.  Ranks split the batch."""
     name = "rope_qk"
     B, S, H, Hk, D = 8, 4096, 32, 8, 128
     interleaved = False
     ROWS_ATTR = "B"
 
-    def setup(self, device, rank, world):
-        import b200k
-        self.b2k = b200k
-        s = 1000 * rank
-        self.q = _randn((self.B, self.S, self.H, self.D), torch.bfloat16, device, s + 31)
-        self.k = _randn((self.B, self.S, self.Hk, self.D), torch.bfloat16, device, s + 32)
-        inv = 10000.0 ** (-torch.arange(0, self.D, 2, device=device, dtype=torch.float32) / self.D)
-        ang = torch.arange(self.S, device=device, dtype=torch.float32)[:, None] * inv[None, :]
+    def make_shared(self):
+        inv = 10000.0 ** (-torch.arange(0, self.D, 2, device=self.device, dtype=torch.float32)
+                          / self.D)
+        ang = torch.arange(self.S, device=self.device, dtype=torch.float32)[:, None] * inv[None, :]
         self.cos = ang.cos().to(torch.bfloat16)
         self.sin = ang.sin().to(torch.bfloat16)
-        self.device = device
 
-    def step(self):
-        return self.b2k.rope_qk(self.q, self.k, self.cos, self.sin, interleaved=self.interleaved)
+    def make_set(self, k):
+        return (_randn((self.rows, self.S, self.H, self.D), torch.bfloat16, self.device,
+                       self.seed(k, 1)),
+                _randn((self.rows, self.S, self.Hk, self.D), torch.bfloat16, self.device,
+                       self.seed(k, 2)))
+
+    def run(self, q, k):
+        return self.b2k.rope_qk(q, k, self.cos, self.sin, interleaved=self.interleaved)
 
     def bytes_per_step(self):
-        qk = (self.B * self.S * (self.H + self.Hk) * self.D) * 2
+        qk = (self.rows * self.S * (self.H + self.Hk) * self.D) * 2
         return 2 * qk + 2 * self.S * (self.D // 2) * 2
 
-    def eager_step(self):
+    def expr(self, q, k):
         # ouroboros/specs.py:96-102 / :228-236 with the tables broadcast over heads
         c = self.cos.float()[None, :, None, :]
         s = self.sin.float()[None, :, None, :]
         out = []
-        for t in (self.q, self.k):
+        for t in (q, k):
             tf = t.float()
             if self.interleaved:
                 o = torch.empty_like(tf)
@@ -563,19 +687,24 @@ class RoPE(Workload):
             out.append(o.to(t.dtype))
         return tuple(out)
 
+    def verify(self, out):
+        want = self.expr(*self.sets[self.last_set])
+        res = [_close(o, w, torch.bfloat16) for o, w in zip(out, want)]
+        return {"parity": all(r[0] for r in res), "max_abs_err": max(r[1] for r in res),
+                "checked": "all of q and k vs the fp32 torch expression"}
+
     def config(self):
         return {"workload": "rope_qk_interleaved" if self.interleaved else "rope_qk_neox",
                 "q": [self.B, self.S, self.H, self.D], "k": [self.B, self.S, self.Hk, self.D],
-                "tables": [self.S, self.D // 2], "theta": 10000.0,
-                "l2": "inputs exceed L2 (336 MB read per step)"}
+                "tables": [self.S, self.D // 2], "theta": 10000.0}
 
     def e2e_setup(self):
-        self.hq = self.q.cpu().pin_memory()
-        self.hk = self.k.cpu().pin_memory()
+        q, k = self.sets[0]
+        self.hq, self.hk = q.cpu().pin_memory(), k.cpu().pin_memory()
         self.hc, self.hs = self.cos.cpu(), self.sin.cpu()
         self.hqo = torch.empty_like(self.hq).pin_memory()
         self.hko = torch.empty_like(self.hk).pin_memory()
-        qk = (self.B * self.S * (self.H + self.Hk) * self.D) * 2
+        qk = (self.rows * self.S * (self.H + self.Hk) * self.D) * 2
         return (qk + 2 * self.S * (self.D // 2) * 2, qk)
 
     def e2e_step(self, timing):
@@ -655,7 +784,7 @@ def run_mlp_block(args, device):
         for _ in range(3):
             fn(*a)
         torch.cuda.synchronize()
-        return time_steps(lambda: fn(*a), max(10, args.steps), stream)[0]
+        return StepTimer(lambda: fn(*a), max(10, args.steps), stream, graph=False).run()
 
     te, to = t(block_eager, *inputs), t(block_ours, *inputs)
     tne, tno = t(nongemm_eager, x, res, w), t(b200k.add_rmsnorm, x, res, w)
@@ -675,8 +804,10 @@ def run_mlp_block(args, device):
 # ---------------------------------------------------------------------------
 # Shape grid (ouroboros/rebench_shapes.py:37-41): every listed op at every
 # (M, N) cell in fp16 and bf16 — b200k GB/s and % of the HBM peak, torch eager
-# time of the reference expression, and a parity check of sampled rows
-# against the CPU oracle.  One JSON line per op.
+# (and, with --grid-compile, torch.compile) time of the reference expression,
+# each timed --repeats times (ouroboros/rebench_stability.py:17-55) with input
+# sets rotated so every call reads from HBM, and a parity check of the whole
+# output against the reference expression.  One JSON line per op.
 MATRIX_GRID = [(1024, 4096), (4096, 4096), (8192, 4096), (4096, 8192), (16384, 2048), (256, 16384)]
 ROPE_GRID = [(8192, 128), (32768, 128), (65536, 64), (16384, 256)]
 
@@ -697,9 +828,23 @@ def _eager_table():
         h = xf.shape[-1] // 2
         return torch.cat([-xf[..., h:], xf[..., :h]], -1)
 
+    def rms(h):
+        return h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-6)
+
+    def rope_inter(x, c, s):
+        xf, cf, sf = x.float(), c.float(), s.float()
+        o = torch.empty_like(xf)
+        o[..., 0::2] = xf[..., 0::2] * cf - xf[..., 1::2] * sf
+        o[..., 1::2] = xf[..., 1::2] * cf + xf[..., 0::2] * sf
+        return o.to(x.dtype)
+
+    def qknorm_rope(x, w, c, s):
+        n = rms(x.float()) * w.float()
+        return (n * c.float() + rot(n) * s.float()).to(x.dtype)
+
     return {  # the expressions of ouroboros/specs.py / chains.py, eager
-        "rmsnorm": lambda x, w: (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype) * w,
-        "rmsnorm_gemma": lambda x, w: (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6) * (1.0 + w.float())).to(x.dtype),
+        "rmsnorm": lambda x, w: rms(x.float()).to(x.dtype) * w,
+        "rmsnorm_gemma": lambda x, w: (rms(x.float()) * (1.0 + w.float())).to(x.dtype),
         "softmax": lambda x: torch.softmax(x.float(), -1).to(x.dtype),
         "log_softmax": lambda x: torch.log_softmax(x.float(), -1).to(x.dtype),
         "softcap_softmax": lambda x: torch.softmax(30.0 * torch.tanh(x.float() / 30.0), -1).to(x.dtype),
@@ -708,23 +853,26 @@ def _eager_table():
         "geglu": lambda g, u: (gelu(g.float()) * u.float()).to(g.dtype),
         "gelu": lambda x: gelu(x.float()).to(x.dtype),
         "silu": lambda x: (x.float() * torch.sigmoid(x.float())).to(x.dtype),
-        "add_rmsnorm": lambda x, r, w: ((x.float() + r.float()) * torch.rsqrt((x.float() + r.float()).pow(2).mean(-1, keepdim=True) + 1e-6)).to(x.dtype) * w,
+        "add_rmsnorm": lambda x, r, w: rms(x.float() + r.float()).to(x.dtype) * w,
         "layernorm": lambda x, w, b: ln(x.float(), w, b).to(x.dtype),
         "add_layernorm": lambda x, r, w, b: ln(x.float() + r.float(), w, b).to(x.dtype),
         "layernorm_gelu": lambda x, w, b: gelu(ln(x.float(), w, b)).to(x.dtype),
         "add_layernorm_gelu": lambda x, r, w, b: gelu(ln(x.float() + r.float(), w, b)).to(x.dtype),
-        "add_rmsnorm_silu": lambda x, r, w: F.silu((x.float() + r.float()) * torch.rsqrt((x.float() + r.float()).pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()).to(x.dtype),
+        "add_rmsnorm_silu": lambda x, r, w: F.silu(rms(x.float() + r.float()) * w.float()).to(x.dtype),
         "cross_entropy": lambda x, t: F.cross_entropy(x.float(), t, reduction="none").to(x.dtype),
         "rope": lambda x, c, s: (x.float() * c.float() + rot(x.float()) * s.float()).to(x.dtype),
-        "rope_interleaved": None,
-        "qknorm_rope": None,
+        "rope_interleaved": rope_inter,
+        "qknorm_rope": qknorm_rope,
     }
 
 
-GRID_OPS = ["rmsnorm", "rmsnorm_gemma", "softmax", "log_softmax", "softcap_softmax", "swiglu",
-            "glu", "geglu", "gelu", "silu", "add_rmsnorm", "layernorm", "add_layernorm",
-            "layernorm_gelu", "add_layernorm_gelu", "add_rmsnorm_silu", "cross_entropy", "rope",
-            "rope_interleaved", "qknorm_rope"]
+# op -> input kind of _grid_inputs
+GRID_OPS = {"rmsnorm": "rms", "rmsnorm_gemma": "rms", "softmax": "x", "log_softmax": "x",
+            "softcap_softmax": "x", "swiglu": "gate_up", "glu": "gate_up", "geglu": "gate_up",
+            "gelu": "x", "silu": "x", "add_rmsnorm": "add_rms", "layernorm": "ln",
+            "add_layernorm": "add_ln", "layernorm_gelu": "ln", "add_layernorm_gelu": "add_ln",
+            "add_rmsnorm_silu": "add_rms", "cross_entropy": "ce", "rope": "rope",
+            "rope_interleaved": "rope_inter", "qknorm_rope": "qkr"}
 
 
 def _grid_inputs(kind, M, N, dt, device, seed):
@@ -753,8 +901,6 @@ def _grid_inputs(kind, M, N, dt, device, seed):
         return (rn(M, N), cos, sin)
     if kind == "qkr":
         return (rn(M, N), rn(N), cos, sin)
-    if kind == "arr":
-        return (rn(M, N), rn(M, N), rn(N), cos, sin)
     raise KeyError(kind)
 
 
@@ -762,95 +908,157 @@ def _algo_bytes(args, out):
     return sum(t.numel() * t.element_size() for t in args) + out.numel() * out.element_size()
 
 
+def _cycle(fn, sets):
+    state = {"i": 0}
+
+    def f():
+        s = sets[state["i"] % len(sets)]
+        state["i"] += 1
+        return fn(*s)
+    return f
+
+
+def _time_cell(fn, sets, stream, repeats):
+    """ms per call (one figure per repeat) of fn over the rotating input sets,
+    from a CUDA graph; stream launches where the expression cannot be
+    captured."""
+    steps = len(sets) * max(1, -(-20 // len(sets)))
+    try:
+        return StepTimer(_cycle(fn, sets), steps, stream, graph=True, hold=len(sets)).run_many(
+            repeats)
+    except Exception:
+        torch.cuda.synchronize()
+        return StepTimer(_cycle(fn, sets), steps, stream, graph=False).run_many(repeats)
+
+
 def run_grid(args, device):
     import b200k
-    from oracle import regimes
-    from oracle.numerics import allclose_report, tol_for
     eager = _eager_table()
     peak, _ = hbm_peak()
     stream = torch.cuda.current_stream(device)
-    ops = args.grid.split(",") if args.grid not in ("1", "all") else GRID_OPS
+    ops = list(GRID_OPS) if args.grid in ("1", "all") else args.grid.split(",")
     tdt = {"fp16": torch.float16, "bf16": torch.bfloat16}
-    odt = {"fp16": "f16", "bf16": "bf16"}
     for op in ops:
-        kind = regimes.OPS[op].kind
-        cells = ROPE_GRID if kind in ("rope", "rope_inter", "qkr", "arr") else MATRIX_GRID
+        kind = GRID_OPS[op]
+        cells = ROPE_GRID if kind in ("rope", "rope_inter", "qkr") else MATRIX_GRID
         if args.cells:
             want = {tuple(int(v) for v in c.split("x")) for c in args.cells.split(",")}
             cells = [c for c in cells if c in want] or sorted(want)
         res = []
         for (M, N) in cells:
             for dname in [d for d in ("fp16", "bf16") if d in args.dtypes.split(",")]:
-                inp = _grid_inputs(kind, M, N, tdt[dname], device, 1000 + M + N)
+                dt = tdt[dname]
+                probe = _grid_inputs(kind, M, N, dt, device, 1000 + M + N)
                 run = b200k.get_op(op)
-                out = run(*inp)
-                # parity: 16 sampled rows against the oracle
-                rows = torch.unique(torch.randint(0, M, (16,), generator=torch.Generator().manual_seed(M)))
-                sub = []
-                for t in inp:
-                    v = t.float().cpu().numpy() if t.is_floating_point() else t.cpu().numpy()
-                    if (t.dim() >= 2 and t.shape[0] == M) or (t.dim() == 1 and not t.is_floating_point()):
-                        v = v[rows.numpy()]
-                    tag = odt[dname] if t.is_floating_point() else "i64"
-                    sub.append((v, tag))
-                ref = regimes.reference(op, sub)
-                got = out.float().cpu().numpy()[rows.numpy()]
-                ok = allclose_report(got, ref, *tol_for(op, odt[dname]))[0]
-                ms, _ = time_steps(lambda: run(*inp), 20, stream, graph_steps=10)
-                nbytes = _algo_bytes(inp, out)
+                out = run(*probe)
+                e = eager[op]
+                ok, err = _close(out, e(*probe), dt)
+                nbytes = _algo_bytes(probe, out)
+                nsets = int(max(1, min(64, -(-ROTATE_BYTES // nbytes))))
+                sets = [probe] + [_grid_inputs(kind, M, N, dt, device, 1000 + M + N + 7 * k)
+                                  for k in range(1, nsets)]
+                ms = _time_cell(run, sets, stream, args.repeats)
+                med = statistics.median(ms)
                 cell = {"M": M, "N": N, "dtype": dname, "parity": bool(ok),
-                        "us": round(ms * 1e3, 2), "GBs": round(nbytes / (ms * 1e-3) / 1e9, 1),
-                        "frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 3)}
-                e = eager.get(op)
-                if e is not None:
-                    e(*inp)
-                    torch.cuda.synchronize()
-                    em, _ = time_steps(lambda: e(*inp), 10, stream, graph_steps=5)
-                    cell["eager_us"] = round(em * 1e3, 2)
-                    cell["speedup_vs_eager"] = round(em / ms, 2)
+                        "max_abs_err": err, "us": round(med * 1e3, 2),
+                        "GBs": round(nbytes / (med * 1e-3) / 1e9, 1),
+                        "frac": round(nbytes / (med * 1e-3) / 1e9 / peak, 3),
+                        "input_sets": nsets}
+                if args.repeats > 1:
+                    cell["us_repeats"] = [round(v * 1e3, 2) for v in ms]
+                    cell["spread"] = round((max(ms) - min(ms)) / med, 4)
+                em = statistics.median(_time_cell(e, sets, stream, 1))
+                cell["eager_us"] = round(em * 1e3, 2)
+                cell["speedup_vs_eager"] = round(em / med, 2)
+                for mode in ([m for m in args.grid_compile.split(",") if m]
+                             if args.grid_compile else []):
+                    key = "compile" if mode == "default" else mode
+                    try:
+                        fn = torch.compile(e, mode=mode, dynamic=False)
+                        for _ in range(3):
+                            fn(*probe)
+                        torch.cuda.synchronize()
+                        cm = statistics.median(_time_cell(fn, sets, stream, 1))
+                        cell[f"{key}_us"] = round(cm * 1e3, 2)
+                        cell[f"speedup_vs_{key}"] = round(cm / med, 2)
+                    except Exception as ex:  # a compiler failure is reported, not fatal
+                        torch.cuda.synchronize()
+                        cell[f"{key}_unavailable"] = f"{type(ex).__name__}: {str(ex)[:100]}"
                 res.append(cell)
-                del inp, out
-        sp = [c["speedup_vs_eager"] for c in res if "speedup_vs_eager" in c]
+                del probe, out, sets
+        sp = [c["speedup_vs_eager"] for c in res]
         geo = float(np.exp(np.mean(np.log(sp)))) if sp else None
-        emit({"op": op, "cells": res, "all_parity": all(c["parity"] for c in res),
-              "geomean_speedup_vs_eager": round(geo, 3) if geo else None,
-              "mean_frac": round(float(np.mean([c["frac"] for c in res])), 3)})
+        line = {"op": op, "cells": res, "all_parity": all(c["parity"] for c in res),
+                "geomean_speedup_vs_eager": round(geo, 3) if geo else None,
+                "mean_frac": round(float(np.mean([c["frac"] for c in res])), 3),
+                "timing": "CUDA graph of >= 20 calls over rotating input sets (>= 3 x L2 "
+                          "between two uses of a set), median of the repeats"}
+        for key in ("compile", "max-autotune-no-cudagraphs"):
+            sp = [c[f"speedup_vs_{key}"] for c in res if f"speedup_vs_{key}" in c]
+            if sp:
+                line[f"geomean_speedup_vs_{key}"] = round(float(np.exp(np.mean(np.log(sp)))), 3)
+        emit(line)
     return 0
 
 
 # ---------------------------------------------------------------------------
 # device timing
-def time_steps(fn, steps, stream, graph_steps=0):
-    """ms per step of fn() over `steps` steps, CUDA events on `stream`.  With
-    graph_steps > 0 the steps are captured into a CUDA graph of graph_steps
-    calls (host launch overhead removed) and the graph is replayed."""
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if graph_steps > 0:
-        g = torch.cuda.CUDAGraph()
-        side = torch.cuda.Stream()
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            for _ in range(graph_steps):
+class StepTimer:
+    """Times `steps` calls of fn() with CUDA events on `stream`.
+
+    graph=True: the calls are captured into one CUDA graph and the graph is
+    replayed (once untimed, then between the events).  During capture the
+    outputs of the last `hold` calls are kept alive, so consecutive calls
+    write distinct buffers (a buffer is reused only every `hold` calls, the
+    same period as the rotating input sets).  `last` is the output of the
+    last call, valid after every replay while the timer lives."""
+
+    def __init__(self, fn, steps, stream, graph=True, hold=1):
+        self.fn, self.steps, self.stream = fn, int(steps), stream
+        self.graph = None
+        self.last = None
+        if graph:
+            side = torch.cuda.Stream()
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):  # warm-up on a side stream before capture
                 fn()
-        stream.wait_stream(side)
-        with torch.cuda.graph(g):
-            for _ in range(graph_steps):
-                fn()
-        reps = max(1, (steps + graph_steps - 1) // graph_steps)
-        g.replay()
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(reps):
+            stream.wait_stream(side)
+            torch.cuda.synchronize()
+            keep = collections.deque(maxlen=max(1, hold))
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(self.steps):
+                    keep.append(fn())
+            self.last = keep[-1]
+            self.graph = g
             g.replay()
-        e1.record(stream)
+            torch.cuda.synchronize()
+
+    def _once(self, pre=None):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if pre is not None:
+            pre()
+        e0.record(self.stream)
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            for _ in range(self.steps):
+                self.last = self.fn()
+        e1.record(self.stream)
         torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / (reps * graph_steps), reps * graph_steps
-    e0.record(stream)
-    for _ in range(steps):
-        fn()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / steps, steps
+        return e0.elapsed_time(e1) / self.steps
+
+    def run(self, pre=None):
+        """ms per call over one timed pass; `pre` (untimed) runs right before
+        the start event."""
+        return self._once(pre)
+
+    def run_many(self, repeats):
+        return [self._once() for _ in range(max(1, repeats))]
+
+    def close(self):
+        self.last = None
+        self.graph = None
 
 
 # ---------------------------------------------------------------------------
@@ -882,36 +1090,90 @@ def cpu_measure(wl, budget_s=10.0, threads=None, rows_per_task=64):
 
 
 # ---------------------------------------------------------------------------
-def measure_device(wl, args, stream, barrier, dist, device, local, sample_clocks=True):
-    """(ms per step max over ranks, ms this rank, steps timed, clock summary)."""
-    for _ in range(args.warmup):
+class Ranks:
+    """The process group plumbing of the bench (None when N = 1)."""
+
+    def __init__(self, dist, device):
+        self.dist, self.device = dist, device
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def gather(self, v):
+        """[v of rank 0, v of rank 1, ...] (floats)."""
+        if self.dist is None:
+            return [float(v)]
+        t = torch.tensor([float(v)], dtype=torch.float64, device=self.device)
+        out = [torch.empty_like(t) for _ in range(self.dist.get_world_size())]
+        self.dist.all_gather(out, t)
+        return [float(o) for o in out]
+
+
+def measure_device(wl, ranks, stream, local, steps, warmup, graph=True):
+    """Times `steps` steps of wl after `warmup` untimed ones and checks the
+    last timed output.  Returns a dict: ms (max over ranks), ms_rank (this
+    rank's), per_rank [min, median, max], clocks, parity record."""
+    for _ in range(warmup):
         wl.step()
     torch.cuda.synchronize()
-    barrier()
+    timer = StepTimer(wl.step, steps, stream, graph=graph and wl.graphable, hold=wl.nsets)
+    captured_last = wl.last_set
+    # ranks whose steps wait for one another (the cross-entropy exchange)
+    # start the timed region together: one untimed exchanging step first
+    pre = wl.step if (wl.world > 1 and getattr(wl, "exchange", "").startswith("peer")) else None
+    ranks.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        ms, steps = time_steps(wl.step, args.steps, stream, wl.graph_steps if args.graph else 0)
-    barrier()
-    ms_max = ms
-    if dist is not None:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
-    return ms_max, ms, steps, clk.summary()
+        ms = timer.run(pre=pre)
+    ranks.barrier()
+    if timer.graph is not None:
+        wl.last_set = captured_last
+    parity = wl.verify(timer.last)
+    launch = "cuda_graph" if timer.graph is not None else "stream"
+    timer.close()
+    per = ranks.gather(ms)
+    ok_all = ranks.gather(1.0 if parity["parity"] else 0.0)
+    parity["parity"] = all(v == 1.0 for v in ok_all)
+    return {"ms": max(per), "ms_rank": ms, "per_rank": per, "clocks": clk.summary(),
+            "check": parity, "launch": launch, "steps": steps}
 
 
 def measure_eager(wl, stream, steps=5):
-    if not hasattr(wl, "eager_step"):
-        return None
     try:
         for _ in range(2):
             wl.eager_step()
         torch.cuda.synchronize()
-        ms, _ = time_steps(wl.eager_step, steps, stream)
-        return ms
+        return StepTimer(wl.eager_step, steps, stream, graph=False).run()
     except torch.cuda.OutOfMemoryError:
         torch.cuda.empty_cache()
         return None
+
+
+def measure_compile(wl, stream, mode, steps=10):
+    """ms per step of the reference expressions under torch.compile (timed
+    from a CUDA graph like the workload's own kernel, stream launches where
+    the compiled code cannot be captured), or a one-line reason when that
+    baseline cannot be had."""
+    try:
+        st = wl.compile_step(mode)
+        if st is None:
+            return None, "not compiled: the step runs autograd"
+        for _ in range(3):  # compiles on the first call
+            st()
+        torch.cuda.synchronize()
+        steps = max(steps, wl.nsets)
+        try:
+            return StepTimer(st, steps, stream, graph=True, hold=wl.nsets).run(), None
+        except Exception:
+            torch.cuda.synchronize()
+        return StepTimer(st, steps, stream, graph=False).run(), None
+    except torch.cuda.OutOfMemoryError:
+        torch.cuda.empty_cache()
+        return None, "out of memory"
+    except Exception as e:  # a compiler failure is reported, not fatal
+        torch.cuda.synchronize()
+        return None, f"{type(e).__name__}: {str(e)[:120]}"
 
 
 _OUT = None
@@ -935,31 +1197,72 @@ def emit(obj):
     print(json.dumps(obj), file=_json_out(), flush=True)
 
 
-def measure_compile(wl, stream, mode, steps=5, graph_steps=0):
-    """ms per step of the reference expressions under torch.compile, or a
-    one-line reason when that baseline cannot be had.  graph_steps > 0 times
-    it from a CUDA graph, as the workload's own kernel is timed."""
-    try:
-        st = wl.compile_step(mode)
-        if st is None:
-            return None, "not compiled: the step runs autograd"
-        for _ in range(3):  # compiles on the first call
-            st()
-        torch.cuda.synchronize()
-        if graph_steps > 0:
-            try:
-                ms, _ = time_steps(st, max(steps, 2 * graph_steps), stream, graph_steps)
-                return ms, None
-            except Exception:
-                torch.cuda.synchronize()
-        ms, _ = time_steps(st, steps, stream)
-        return ms, None
-    except torch.cuda.OutOfMemoryError:
-        torch.cuda.empty_cache()
-        return None, "out of memory"
-    except Exception as e:  # a compiler failure is reported, not fatal
-        torch.cuda.synchronize()
-        return None, f"{type(e).__name__}: {str(e)[:120]}"
+COMPILE_MODES = ("default", "max-autotune-no-cudagraphs")
+
+
+def _baselines(wl, stream, args, ms_rank, world, entry):
+    """Adds the eager and torch.compile baselines of wl to `entry` (the
+    compile modes at N = 1 only: compiling per rank adds minutes and no
+    information)."""
+    if not args.no_eager:
+        e = measure_eager(wl, stream, 3 if wl.bytes_per_step() > (1 << 30) else 5)
+        if e is not None:
+            entry["eager_ms_per_step"] = round(e, 5)
+            entry["speedup_vs_eager"] = round(e / ms_rank, 3)
+    if args.no_compile or (world > 1 and not args.compile_all_ranks):
+        return
+    for mode in [m for m in args.compile_modes.split(",") if m]:
+        key = "compile" if mode == "default" else "max_autotune"
+        c, why = measure_compile(wl, stream, mode)
+        if c:
+            entry[f"{key}_ms_per_step"] = round(c, 5)
+            entry[f"speedup_vs_{key}"] = round(c / ms_rank, 3)
+        else:
+            entry[f"{key}_unavailable"] = why
+        torch._dynamo.reset()
+
+
+def _ce_parts(wl, stream, steps):
+    """Cross-entropy step split into its kernels: the row-loss kernel alone
+    (b200k.cross_entropy, per-row losses) against the whole step."""
+    x, t = wl.sets[0]
+    f = lambda: wl.b2k.cross_entropy(x, t)
+    f()
+    torch.cuda.synchronize()
+    return StepTimer(f, steps, stream, graph=True).run()
+
+
+def run_config(name, wl, args, ranks, stream, local, steps, warmup, peak, world):
+    """Measures one workload; returns its JSON entry (and keeps the figures
+    the headline needs in entry['_raw'])."""
+    r = measure_device(wl, ranks, stream, local, steps, warmup, graph=bool(args.graph))
+    bytes_rank = wl.bytes_per_step()
+    total = sum(ranks.gather(bytes_rank))
+    per = sorted(r["per_rank"])
+    entry = {"value": round(total / (r["ms"] * 1e-3) / 1e9, 2), "unit": "GB/s",
+             "ms_per_step": round(r["ms"], 5),
+             "frac": round(bytes_rank / (r["ms_rank"] * 1e-3) / 1e9 / peak, 4),
+             "per_rank_ms": {"min": round(per[0], 5), "median": round(statistics.median(per), 5),
+                             "max": round(per[-1], 5)},
+             "parity": r["check"]["parity"], "check": r["check"],
+             "scaling": wl.scaling, "config": wl.config(), "rows_per_rank": wl.rows,
+             "input_sets": wl.nsets, "launch": r["launch"], "steps": steps,
+             "gpu_launches": steps * wl.launches_per_step}
+    if hasattr(wl, "bytes_needed"):
+        need = wl.bytes_needed()
+        entry["bytes_needed"] = need
+        entry["frac_on_bytes_needed"] = round(need / (r["ms_rank"] * 1e-3) / 1e9 / peak, 4)
+    if isinstance(wl, CrossEntropy) and type(wl) is CrossEntropy:
+        entry["exchange"] = wl.exchange
+        if wl.exchange.startswith("peer"):
+            from b200k.dist import exchange_status
+            entry["exchange_status"] = exchange_status(None, wl.device)
+        rk = _ce_parts(wl, stream, steps)
+        entry["row_kernel_ms"] = round(rk, 5)
+        entry["reduce_exchange_ms"] = round(max(0.0, r["ms_rank"] - rk), 5)
+    entry["_raw"] = r
+    entry["_bytes_rank"] = bytes_rank
+    return entry
 
 
 def main():
@@ -974,22 +1277,26 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
-                    help="skip the device-only measurement of the other configurations")
+                    help="skip the measurement of the other configurations")
+    ap.add_argument("--extra-steps", type=int, default=100,
+                    help="timed steps of each other configuration")
     ap.add_argument("--no-eager", action="store_true")
     ap.add_argument("--no-compile", action="store_true",
-                    help="skip the torch.compile baseline of the headline workload")
-    ap.add_argument("--compile", action="store_true",
-                    help="also time the torch.compile baseline of the other configurations")
-    ap.add_argument("--compile-mode", default="default",
-                    help="torch.compile mode of the baseline (the reference harness's strong "
-                         "baseline is max-autotune-no-cudagraphs)")
+                    help="skip the torch.compile baselines")
+    ap.add_argument("--compile-modes", default=",".join(COMPILE_MODES),
+                    help="torch.compile modes timed as baselines (N = 1)")
+    ap.add_argument("--compile-all-ranks", action="store_true",
+                    help="also time the compile baselines when N > 1")
     ap.add_argument("--graph", type=int, default=1,
-                    help="launch small workloads from a CUDA graph (1) or one by one (0)")
+                    help="time the steps from a CUDA graph (1) or launch them one by one (0)")
     ap.add_argument("--grid", default="",
                     help="shape-grid mode: comma list of ops (or 'all'); one JSON line per op")
     ap.add_argument("--cells", default="",
                     help="grid mode: only these shapes, comma list of MxN (e.g. 32768x128)")
     ap.add_argument("--dtypes", default="fp16,bf16", help="grid mode: dtypes to run")
+    ap.add_argument("--repeats", type=int, default=1, help="grid mode: timings per cell")
+    ap.add_argument("--grid-compile", default="",
+                    help="grid mode: comma list of torch.compile modes to time per cell")
     ap.add_argument("--rows", type=int, default=0,
                     help="override the row count of the workload (M; batch for rope; "
                          "tokens for ce) — small cases for profiler captures")
@@ -1001,7 +1308,6 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.grid:
         torch.cuda.set_device(local)
-        sys.path.insert(0, ROOT)
         sys.exit(run_grid(args, torch.device("cuda", local)))
     if args.workload == "mlp_block":
         torch.cuda.set_device(local)
@@ -1021,40 +1327,22 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-
+    ranks = Ranks(dist, device)
     stream = torch.cuda.current_stream(device)
-    wl.setup(device, rank, world)
-    ms_max, ms, steps_timed, clocks = measure_device(wl, args, stream, barrier, dist, device, local)
-
-    # every rank's bytes_per_step is its own share (a full configuration for
-    # the weakly scaled workloads, its row shard for ce), so the job moves
-    # world x that per step
-    total_bytes = wl.bytes_per_step() * world
-    value = total_bytes / (ms_max * 1e-3) / 1e9
     peak, peak_kind = hbm_peak()
-    # the dominant kernel is timed with its step (any small companion
-    # kernels of the step count against it, which only lowers the figure)
-    achieved = wl.bytes_per_step() / (ms * 1e-3) / 1e9
 
-    eager = None
-    if not args.no_eager:
-        e_ms = measure_eager(wl, stream)
-        if e_ms is not None:
-            eager = {"ms_per_step": round(e_ms, 4), "speedup": round(e_ms / ms, 2),
-                     "what": "the reference's PyTorch expressions (ouroboros/specs.py), eager"}
-    compiled = None
-    if not args.no_compile:
-        c_ms, why = measure_compile(wl, stream, args.compile_mode,
-                                    graph_steps=wl.graph_steps if args.graph else 0)
-        compiled = ({"ms_per_step": round(c_ms, 4), "speedup": round(c_ms / ms, 2)} if c_ms
-                    else {"unavailable": why})
-        compiled.update({"mode": args.compile_mode,
-                         "what": "the same expressions under torch.compile (the reference "
-                                 "harness's baseline)"})
+    wl.setup(device, rank, world)
+    wl.poke()
+    head = run_config(wl.name, wl, args, ranks, stream, local, args.steps, args.warmup, peak,
+                      world)
+    raw = head.pop("_raw")
+    bytes_rank = head.pop("_bytes_rank")
+    ms_max, ms = raw["ms"], raw["ms_rank"]
+    total_bytes = sum(ranks.gather(bytes_rank))
+    value = total_bytes / (ms_max * 1e-3) / 1e9
+    achieved = bytes_rank / (ms * 1e-3) / 1e9  # this rank's kernel: bytes / launch time
+    base = {}
+    _baselines(wl, stream, args, ms, world, base)
 
     # end to end through the host-buffer API (pinned host in, pinned host out)
     e2e = None
@@ -1063,17 +1351,13 @@ def main():
         times = []
         for i in range(3 + max(3, min(args.steps, 10))):
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            barrier()
+            ranks.barrier()
             wl.e2e_step(ev)
             if i >= 3:
                 times.append(ev[0].elapsed_time(ev[1]))
-        e_ms = statistics.median(times)
-        if dist is not None:
-            t = torch.tensor([e_ms], device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = float(t.item())
+        e_ms = max(ranks.gather(statistics.median(times)))
         e_bytes = wl.e2e_bytes() if hasattr(wl, "e2e_bytes") else wl.bytes_per_step()
-        e_total = e_bytes * world
+        e_total = sum(ranks.gather(e_bytes))
         e2e = {"value": round(e_total / (e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                "ms_per_step": round(e_ms, 4), "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "api": wl.e2e_api()}
@@ -1094,70 +1378,59 @@ def main():
         except Exception:
             traffic = None
 
-    # the fields of the line that need the configured workload
-    wl_cfg, wl_bytes = wl.config(), wl.bytes_per_step()
-    wl_scaling, wl_dtype, wl_graph = wl.scaling, wl.dtype, wl.graph_steps
-
-    # the other named configurations, device time only
+    wl_cfg, wl_scaling, wl_dtype = wl.config(), wl.scaling, wl.dtype
+    launches = args.steps * wl.launches_per_step
+    del wl
+    torch.cuda.empty_cache()
     extra = {}
-    # kernels of this library launched inside the headline timed region
-    launches = steps_timed * wl.launches_per_step
     if not args.no_extra:
-        del wl
-        torch.cuda.empty_cache()
         for name in ("rmsnorm", "swiglu", "rope", "rope_interleaved", "ce"):
             if name == args.workload:
                 continue
             w2 = WORKLOADS[name]()
             w2.setup(device, rank, world)  # full configuration (no --rows)
-            a2 = argparse.Namespace(**vars(args))
-            a2.steps, a2.warmup = (40 if name != "ce" else 10), 5
-            m2, m2_local, st2, ck2 = measure_device(w2, a2, stream, barrier, dist, device, local)
-            tb = w2.bytes_per_step() * world
-            per_rank = w2.bytes_per_step() / (m2_local * 1e-3) / 1e9
-            entry = {"value": round(tb / (m2 * 1e-3) / 1e9, 2), "unit": "GB/s",
-                     "ms_per_step": round(m2, 5), "frac": round(per_rank / peak, 4),
-                     "scaling": w2.scaling, "config": w2.config(),
-                     "launch": "cuda_graph" if (args.graph and w2.graph_steps) else "stream",
-                     "gpu_launches": st2 * w2.launches_per_step}
-            if not args.no_eager:
-                e2 = measure_eager(w2, stream, 3)
-                if e2 is not None:
-                    entry["eager_ms_per_step"] = round(e2, 4)
-                    entry["speedup_vs_eager"] = round(e2 / m2_local, 2)
-            if args.compile:
-                c2, why = measure_compile(w2, stream, args.compile_mode, 3,
-                                          w2.graph_steps if args.graph else 0)
-                if c2:
-                    entry["compile_ms_per_step"] = round(c2, 4)
-                    entry["speedup_vs_compile"] = round(c2 / m2_local, 2)
-                else:
-                    entry["compile_unavailable"] = why
+            w2.poke()
+            steps2 = max(args.extra_steps, w2.nsets)
+            entry = run_config(w2.name, w2, args, ranks, stream, local, steps2, 5, peak, world)
+            m2 = entry.pop("_raw")["ms_rank"]
+            entry.pop("_bytes_rank")
+            if name == "rmsnorm" and args.graph:
+                # the same steps launched one by one from the host
+                r = measure_device(w2, ranks, stream, local, steps2, 3, graph=False)
+                entry["stream_launch"] = {
+                    "ms_per_step": round(r["ms"], 5),
+                    "frac": round(w2.bytes_per_step() / (r["ms_rank"] * 1e-3) / 1e9 / peak, 4),
+                    "parity": r["check"]["parity"]}
+            _baselines(w2, stream, args, m2, world, entry)
             extra[w2.name] = entry
             del w2
             torch.cuda.empty_cache()
-    else:
-        del wl
 
     line = {
         "metric": "achieved HBM GB/s (algorithmic bytes / step time), aggregate over GPUs",
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True,
         "scaling": wl_scaling, "vs_baseline": None, "dtype": wl_dtype, "data": "synthetic",
-        "config": dict(wl_cfg, parallelism=f"rows x{world}" if world > 1 else "1 GPU",
-                       launch="cuda_graph" if (args.graph and wl_graph) else "stream"),
+        "config": dict(wl_cfg, parallelism=f"rows split over {world} GPUs" if world > 1
+                       else "1 GPU", launch=head["launch"],
+                       l2=f"{head['input_sets']} rotating input set(s) per rank: >= 3 x L2 of "
+                          "traffic between two uses of a set"),
+        "parity": head["parity"], "check": head["check"],
+        "per_rank_ms": head["per_rank_ms"], "rows_per_rank": head["rows_per_rank"],
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "peak_source": peak_kind,
-                     "algorithmic_bytes_per_launch": wl_bytes},
+                     "peak_source": peak_kind, "algorithmic_bytes_per_launch": bytes_rank},
         "e2e": e2e,
         "cpu_baseline": cpu,
-        "eager": eager,
-        "compile": compiled,
+        "baselines": base or None,
         "gpu_launches": launches,
-        "clocks": clocks,
+        "clocks": raw["clocks"],
         "other_configs": extra or None,
     }
+    for k in ("bytes_needed", "frac_on_bytes_needed", "exchange", "exchange_status",
+              "row_kernel_ms", "reduce_exchange_ms"):
+        if k in head:
+            line[k] = head[k]
     if rank == 0:
         emit(line)
     if dist is not None:

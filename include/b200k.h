@@ -19,7 +19,9 @@
  *   - launches go on `stream` (a cudaStream_t, NULL = legacy default stream),
  *     nothing synchronises the host;
  *   - the return value is a b2k_status; on failure b2k_last_error() returns a
- *     thread-local message.  No entry point allocates device memory.
+ *     thread-local message.  No compute entry point allocates device memory;
+ *     the one allocating call is b2k_ce_exchange_alloc, the set-up of the
+ *     multi-GPU cross-entropy exchange buffer (freed by b2k_ce_exchange_free).
  */
 #ifndef B200K_H
 #define B200K_H
@@ -256,9 +258,11 @@ int b2k_cross_entropy_fwd_bwd(const void* x, int64_t ldx, const int64_t* tgt, in
  * that loads it), so the caller passes only inputs and the output and
  * nothing is allocated.  M above B2K_NOALLOC_MAX_ROWS is rejected with
  * B2K_EINVAL.  The first call on a device looks up the buffer's device
- * address (make it before any stream capture); calls whose GPU work overlaps
- * share the buffer and race.  No counterpart in the reference: its kernels
- * allocate their outputs through PyTorch. */
+ * address (make it before any stream capture) and keeps it: after a
+ * cudaDeviceReset of that device the cached address is stale, so do not call
+ * this entry point there again.  Calls whose GPU work overlaps share the
+ * buffer and race.  No counterpart in the reference: its kernels allocate
+ * their outputs through PyTorch. */
 int b2k_cross_entropy_mean_noalloc(const void* x, int64_t ldx, const int64_t* tgt,
                                    int64_t M, int64_t N, int dtype,
                                    int64_t ignore_index, float* out, void* stream);

@@ -115,11 +115,51 @@ class CeExchange:
                     self.opened.append(q.value)
                     ptrs.append(q.value)
                 self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
+                # sticky failure word of the exchange kernel (0 = healthy) and
+                # its copy in pinned host memory, read without a host sync
                 self.status = torch.zeros(1, dtype=torch.int32, device=device)
+                self.status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+                self.status_event = torch.cuda.Event()
+                self.failed = 0
                 torch.cuda.synchronize(device)
                 self.ok = True
             except Exception:
                 self.ok = False
+
+    _WHY = {1: "a rank's wait for the others' [loss sum, valid count] ran out",
+            2: "a peer ran two steps ahead (it had given up waiting)"}
+
+    def _raise(self, v):
+        self.failed = v
+        raise L.B200KError(
+            f"b200k: the cross-entropy exchange of rank {self.rank}/{self.world} failed "
+            f"(status {v}: {self._WHY.get(v, 'unknown')}); its means since then are NaN. "
+            "Set up the process group and the exchange again (close_exchanges()).")
+
+    def raise_if_failed(self):
+        """Raises if an earlier call on this rank reported a failure.  Reads
+        the status copied after the previous call only once that copy has
+        completed (no host synchronisation)."""
+        if self.failed:
+            self._raise(self.failed)
+        if self.status_event.query():
+            v = int(self.status_host[0])
+            if v:
+                self._raise(v)
+
+    def after_launch(self):
+        """Queues, on the current stream, the copy of the status word to pinned
+        host memory (skipped while the stream is being captured into a CUDA
+        graph; exchange_status() reads it after a replay)."""
+        if torch.cuda.is_current_stream_capturing():
+            return
+        self.status_host.copy_(self.status, non_blocking=True)
+        self.status_event.record(torch.cuda.current_stream(self.device))
+
+    def check_now(self) -> int:
+        """Synchronises the device and returns the status word (0 = healthy)."""
+        torch.cuda.synchronize(self.device)
+        return int(self.status.item())
 
     def close(self):
         """Unmap the peers' buffers and free this rank's (after the last use)."""
@@ -160,3 +200,16 @@ def ce_exchange(group, device):
                 x.close()
                 _XCHG[key] = None
         return _XCHG[key]
+
+
+def exchange_status(group=None, device=None) -> int | None:
+    """The status word of the cached cross-entropy exchange of (group,
+    device) after a device synchronisation: 0 healthy, 1 a wait ran out, 2 a
+    peer ran ahead; None when no peer-memory exchange is in use."""
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()):
+        return None
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    _, name = _group_key(group)
+    x = _XCHG.get((name, device.index))
+    return None if x is None else x.check_now()

@@ -539,11 +539,14 @@ def cross_entropy_mean(logits, tgt, ignore_index: int = -100, group=None):
                                      ignore_index, stream)
         L.check(st, "b2k_cross_entropy")
         if xchg is not None:
-            # reduce + exchange over peer memory + mean, one kernel
+            # reduce + exchange over peer memory + mean, one kernel; a failure
+            # reported by an earlier call raises here (sticky on the device)
+            xchg.raise_if_failed()
             L.check(L.lib.b2k_ce_reduce_exchange_mean(
                 _p(row_loss), _p(t1), m, ignore_index, _p(xchg.peers), xchg.rank, xchg.world,
                 XCHG_LIMIT_NS, _p(sumcount), _p(out), _p(xchg.status), stream),
                 "b2k_ce_reduce_exchange_mean")
+            xchg.after_launch()
             return out
         L.check(L.lib.b2k_ce_reduce(_p(row_loss), _p(t1), m, ignore_index, _p(sumcount), stream),
                 "b2k_ce_reduce")

@@ -54,6 +54,7 @@ struct NormArgs {
   int tma_cps;     // CTAs per SM of the bulk-copy path (0 = automatic)
   int tma_stages;  // pipeline depth (0 = automatic)
   int use_tma;     // 0 disables the bulk-copy path
+  int64_t l2_prefetch_bytes;  // bulk-copy path: L2 prefetch budget of one launch (0 = off)
 };
 
 constexpr int kNormMaxThreads = 512;
@@ -364,10 +365,12 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
   const int N = (int)a.N;
   if (g.tx == 0) abort_flag = 0;
   griddep_launch_dependents();
-  griddep_wait();  // inputs may come from the previous kernel in the stream
-  RowPipe<NIN> pipe;
   const void* srcs[2] = {a.x, a.r};
   const int64_t lds[2] = {a.ldx, a.ldr};
+  RowPipe<NIN>::prefetch_l2(srcs, lds, (int)sizeof(T), (uint32_t)N * (uint32_t)sizeof(T), a.M,
+                            a.l2_prefetch_bytes);
+  griddep_wait();  // inputs may come from the previous kernel in the stream
+  RowPipe<NIN> pipe;
   pipe.init(dsm, S, a.M, (uint32_t)N * (uint32_t)sizeof(T), srcs, lds, (int)sizeof(T));
 
   // weight slices stay in registers (raw 16-byte vectors) for every row

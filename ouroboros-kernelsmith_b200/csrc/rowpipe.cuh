@@ -81,6 +81,27 @@ struct RowPipe {
 
   __device__ __forceinline__ int64_t row_of(int64_t k) const { return first + k * stride; }
 
+  // Thread 0: L2 prefetch hints for the first rows of this block, as many as
+  // budget_bytes spread over the grid allow.  Needs no barrier or shared
+  // memory, so a kernel calls it before griddep_wait(): the DRAM reads of its
+  // first rows then overlap the tail of the previous kernel in the stream,
+  // and the bulk copies of those rows find them in L2.
+  __device__ static void prefetch_l2(const void* const* srcs, const int64_t* ld_elems,
+                                     int elem_bytes, uint32_t rbytes, int64_t M,
+                                     int64_t budget_bytes) {
+    if (budget_bytes <= 0 || threadIdx.x != 0 || threadIdx.y != 0) return;
+    const int64_t b = blockIdx.x, g = gridDim.x;
+    const int64_t mine = b < M ? (M - 1 - b) / g + 1 : 0;
+    int64_t n = budget_bytes / (g * (int64_t)NIN * rbytes);
+    if (n > mine) n = mine;
+    for (int64_t k = 0; k < n; ++k)
+#pragma unroll
+      for (int i = 0; i < NIN; ++i)
+        bulk_prefetch_l2(static_cast<const unsigned char*>(srcs[i]) +
+                             (b + k * g) * ld_elems[i] * elem_bytes,
+                         rbytes);
+  }
+
   // Bounded wait for the next row (rows are consumed in order 0, 1, ...);
   // returns the stage base, ok=false on timeout.
   __device__ __forceinline__ const unsigned char* wait_next(bool& ok) {
@@ -145,25 +166,31 @@ inline void launch_pdl(Kernel kern, unsigned grid, unsigned block, size_t smem,
   cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-// Raises the kernel's dynamic shared-memory cap once (to the whole per-block
-// maximum); the launch itself asks for what it needs.
+// Raises the kernel's dynamic shared-memory cap once per device (to the whole
+// per-block maximum); the launch itself asks for what it needs.  The
+// attribute belongs to the current device's context, so a process that
+// launches on several GPUs sets it on each.
 template <typename Kernel>
 inline void allow_max_dynamic_smem(Kernel kern) {
   static std::mutex mu;
-  static const void* done[256];
+  static const void* done[512];
+  static int done_dev[512];
   static int ndone = 0;
-  std::lock_guard<std::mutex> lock(mu);
-  for (int i = 0; i < ndone; ++i)
-    if (done[i] == (const void*)kern) return;
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < ndone; ++i)
+    if (done[i] == (const void*)kern && done_dev[i] == dev) return;
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   cudaFuncAttributes fa;
   cudaFuncGetAttributes(&fa, kern);
   const int cap = optin - (int)fa.sharedSizeBytes;
   if (cap > 0) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
   cudaGetLastError();
-  if (ndone < 256) done[ndone++] = (const void*)kern;
+  if (ndone < 512) {
+    done[ndone] = (const void*)kern;
+    done_dev[ndone++] = dev;
+  }
 }
 
 template <typename Kernel>
@@ -201,14 +228,14 @@ inline bool choose_pipe_shape_uncached(Kernel kern, int threads, int64_t stage_b
   return false;
 }
 
-// Cached per (kernel, threads, stage bytes, overrides): the occupancy query
-// runs once, later launches pay a table lookup.
+// Cached per (device, kernel, threads, stage bytes, overrides): the occupancy
+// query runs once, later launches pay a table lookup.
 template <typename Kernel>
 inline bool choose_pipe_shape(Kernel kern, int threads, int64_t stage_bytes, int want_cps,
                               int want_stages, PipeShape* ps) {
   struct Entry {
     const void* k;
-    int threads, cps, stages;
+    int dev, threads, cps, stages;
     int64_t stage;
     PipeShape ps;
     bool ok;
@@ -216,13 +243,15 @@ inline bool choose_pipe_shape(Kernel kern, int threads, int64_t stage_bytes, int
   static std::mutex mu;
   static Entry cache[512];
   static int n = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
   allow_max_dynamic_smem(kern);
   {
     std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < n; ++i) {
       const Entry& e = cache[i];
-      if (e.k == (const void*)kern && e.threads == threads && e.stage == stage_bytes &&
-          e.cps == want_cps && e.stages == want_stages) {
+      if (e.k == (const void*)kern && e.dev == dev && e.threads == threads &&
+          e.stage == stage_bytes && e.cps == want_cps && e.stages == want_stages) {
         *ps = e.ps;
         return e.ok;
       }
@@ -231,7 +260,8 @@ inline bool choose_pipe_shape(Kernel kern, int threads, int64_t stage_bytes, int
   PipeShape r{1, 2};
   const bool ok = choose_pipe_shape_uncached(kern, threads, stage_bytes, want_cps, want_stages, &r);
   std::lock_guard<std::mutex> lock(mu);
-  if (n < 512) cache[n++] = Entry{(const void*)kern, threads, want_cps, want_stages, stage_bytes, r, ok};
+  if (n < 512)
+    cache[n++] = Entry{(const void*)kern, dev, threads, want_cps, want_stages, stage_bytes, r, ok};
   *ps = r;
   return ok;
 }

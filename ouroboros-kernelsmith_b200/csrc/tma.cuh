@@ -60,6 +60,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// L2 prefetch hint for `bytes` (multiple of 16) at a 16-byte aligned address
+// of this GPU's global memory: no data reaches the block and nothing
+// completes on a barrier.  L2 is the GPU's point of coherence, so a line
+// prefetched before another kernel writes it holds the written data
+// afterwards; the hint never makes a later read stale.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // L2 eviction-priority policies for bulk copies (createpolicy, sm_80+)
 __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;

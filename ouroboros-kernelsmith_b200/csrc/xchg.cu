@@ -19,6 +19,16 @@
 // peer only during call e + 2, after its own wait of call e + 1, which needs
 // the peer's flag of e + 1, which the peer publishes only after it finished
 // reading the pairs of call e (stream order on the peer).
+//
+// That argument holds while no wait gives up.  A rank whose wait ran out may
+// step on and reach call e + 2 while a slow peer is still in call e, so:
+//  * a flag ABOVE the waiting rank's epoch can only come from such a rank;
+//    it is an error (status 2), never accepted as "arrived";
+//  * the status word is sticky: once nonzero (1 = wait ran out, 2 = a peer
+//    ran ahead) every later call of that rank returns NaN without writing
+//    into any peer's buffer, so its peers time out in turn and every rank
+//    ends in the failed state instead of mixing epochs.  The host reads the
+//    word (b200k raises) and the exchange has to be set up again.
 #include <string.h>
 
 #include "tma.cuh"
@@ -52,8 +62,17 @@ __global__ void __launch_bounds__(1024) ce_reduce_exchange_mean_kernel(
     unsigned char* const* peers, int rank, int world, unsigned long long limit_ns,
     double* sumcount, float* out, int* status) {
   __shared__ double rs[32], rc[32];
-  __shared__ int timed_out;
+  __shared__ int timed_out, ran_ahead;
   __shared__ unsigned long long epoch_s;
+  // a failed exchange stays failed (sticky status): no pair is published
+  if (*reinterpret_cast<volatile int*>(status) != 0) {
+    if (threadIdx.x == 0) {
+      sumcount[0] = __longlong_as_double(0x7ff8000000000000ll);
+      sumcount[1] = 0.0;
+      out[0] = __int_as_float(0x7fc00000);
+    }
+    return;
+  }
   double s = 0.0, c = 0.0;
   for (int64_t i = threadIdx.x; i < M; i += blockDim.x) {
     if (tgt[i] != ignore) { s += (double)loss[i]; c += 1.0; }
@@ -64,7 +83,7 @@ __global__ void __launch_bounds__(1024) ce_reduce_exchange_mean_kernel(
     c += __shfl_xor_sync(0xffffffffu, c, o);
   }
   if ((threadIdx.x & 31) == 0) { rs[threadIdx.x >> 5] = s; rc[threadIdx.x >> 5] = c; }
-  if (threadIdx.x == 0) timed_out = 0;
+  if (threadIdx.x == 0) { timed_out = 0; ran_ahead = 0; }
   __syncthreads();
   unsigned char* mine = peers[rank];
   if (threadIdx.x == 0) {
@@ -92,22 +111,25 @@ __global__ void __launch_bounds__(1024) ce_reduce_exchange_mean_kernel(
   if (threadIdx.x < world) {
     const unsigned long long* flag =
         reinterpret_cast<const unsigned long long*>(mine + xchg_flag_off(par, world, threadIdx.x));
-    if (ld_acquire_sys_u64(flag) < epoch) {
+    unsigned long long f = ld_acquire_sys_u64(flag);
+    if (f < epoch) {
       const unsigned long long t0 = globaltimer();
       for (uint32_t i = 1;; ++i) {
-        if (ld_acquire_sys_u64(flag) >= epoch) break;
+        f = ld_acquire_sys_u64(flag);
+        if (f >= epoch) break;
         if ((i & 63u) == 0 && globaltimer() - t0 > limit_ns) {
           atomicExch(&timed_out, 1);
           break;
         }
       }
     }
+    if (f > epoch) atomicExch(&ran_ahead, 1);  // a peer two calls ahead: see above
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    if (timed_out) {
+    if (timed_out || ran_ahead) {
       atomicAdd(&b2k_tu_timeouts, 1u);
-      *status = 1;
+      *status = ran_ahead ? 2 : 1;
       sumcount[0] = __longlong_as_double(0x7ff8000000000000ll);
       sumcount[1] = 0.0;
       out[0] = __int_as_float(0x7fc00000);
@@ -124,7 +146,6 @@ __global__ void __launch_bounds__(1024) ce_reduce_exchange_mean_kernel(
       sumcount[0] = S;
       sumcount[1] = C;
       out[0] = (float)(S / C);  // 0/0 -> NaN (no valid row anywhere)
-      *status = 0;
     }
   }
 }

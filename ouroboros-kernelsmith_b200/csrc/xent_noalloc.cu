@@ -15,7 +15,11 @@
 // use the array's name as a device address (in host code it names a host-side
 // stand-in); the device address is obtained once per device with
 // cudaGetSymbolAddress, with that device current, on the first call made on
-// that device.  Make that first call before any stream capture.  All calls
+// that device.  Make that first call before any stream capture.  The cached
+// address belongs to the device's context at that first call: a process that
+// resets a device (cudaDeviceReset) must not call this entry point on that
+// device afterwards, because the cached address is not looked up again.  All
+// calls
 // share the one buffer: two calls whose work overlaps on the GPU (different
 // streams, or different host threads on the same device) race and give wrong
 // results.  Nothing in the buffer needs clearing between calls: every row
@@ -29,8 +33,9 @@ namespace {
 constexpr int64_t kNoallocMaxRows = B2K_NOALLOC_MAX_ROWS;
 constexpr size_t kLossBytes = (size_t)kNoallocMaxRows * sizeof(float);  // 1 MiB
 
+constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void* g_dev_ptr[64] = {nullptr};
+void* g_dev_ptr[kMaxDevices] = {nullptr};
 
 }  // namespace
 
@@ -51,10 +56,15 @@ extern "C" int b2k_cross_entropy_mean_noalloc(const void* x, int64_t ldx, const 
   B2K_REQUIRE(out != nullptr, "b2k_cross_entropy_mean_noalloc: null output");
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+  if (e != cudaSuccess) {
     b2k::set_error("b2k_cross_entropy_mean_noalloc: cudaGetDevice failed: %s",
                    cudaGetErrorString(e));
     return B2K_ELAUNCH;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    b2k::set_error("b2k_cross_entropy_mean_noalloc: device %d outside the %d devices this "
+                   "entry point keeps scratch addresses for", dev, kMaxDevices);
+    return B2K_EINVAL;
   }
   void* base;
   {

@@ -261,3 +261,20 @@ def test_rope_qk_interleaved_8byte_tables(dt):
         torch.cuda.synchronize()
         _close(qo, rq, dt)
         _close(ko, rk, dt)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_devices_in_one_process():
+    """Per-device launch set-up (the raised shared-memory limit and the cached
+    pipeline shape belong to each device's context): rows of 64 KB, whose
+    pipeline needs more than 48 KB of shared memory, on cuda:0 then cuda:1."""
+    x = _randn((512, 16384), "f32", 1.0, 5)
+    w = _randn((16384,), "f32", 0.1, 6) + 1
+    ref = O.rmsnorm(x, w, "f32")
+    for d in (0, 1):
+        xt = torch.from_numpy(x).to(f"cuda:{d}")
+        wt = torch.from_numpy(w).to(f"cuda:{d}")
+        y = b200k.rmsnorm(xt, wt)
+        torch.cuda.synchronize(d)
+        ok, err, bad = allclose_report(y.cpu().numpy(), ref, *tol_for("rmsnorm", "f32"))
+        assert ok, f"cuda:{d}: max err {err}, {bad} bad"

@@ -32,10 +32,18 @@ def _loss_rows(M=3000, V=4096, seed=3):
     return x, t, row
 
 
-def _call(row, t, peers, rank, world, limit_ns):
+def _call(row, t, peers, rank, world, limit_ns, status=None):
     sc = torch.empty(2, dtype=torch.float64, device="cuda")
     out = torch.empty((), dtype=torch.float32, device="cuda")
-    status = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    if status is not None:
+        st = _lib.lib.b2k_ce_reduce_exchange_mean(
+            row.data_ptr(), t.data_ptr(), row.numel(), -100, peers.data_ptr(), rank, world,
+            limit_ns, sc.data_ptr(), out.data_ptr(), status.data_ptr(),
+            torch.cuda.current_stream().cuda_stream)
+        assert st == _lib.OK, _lib.last_error()
+        torch.cuda.synchronize()
+        return sc, out, int(status.item())
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")
     st = _lib.lib.b2k_ce_reduce_exchange_mean(
         row.data_ptr(), t.data_ptr(), row.numel(), -100, peers.data_ptr(), rank, world, limit_ns,
         sc.data_ptr(), out.data_ptr(), status.data_ptr(), torch.cuda.current_stream().cuda_stream)
@@ -76,6 +84,45 @@ def test_missing_rank_times_out_and_context_survives():
     x, t2, _ = _loss_rows(M=64, seed=4)
     assert np.isfinite(float(b200k.cross_entropy_mean(x, t2)))
     assert _lib.lib.b2k_pipeline_timeouts(1) == 0
+
+
+def test_failed_exchange_stays_failed_and_writes_nothing():
+    """After a wait ran out, the status word is sticky: the next call with it
+    returns NaN at once, publishes nothing into any buffer and leaves the
+    epoch counter alone."""
+    _lib.lib.b2k_pipeline_timeouts(1)
+    _, t, row = _loss_rows(M=500)
+    nb = int(_lib.lib.b2k_ce_exchange_bytes(2))
+    mine = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+    other = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+    peers = torch.tensor([mine.data_ptr(), other.data_ptr()], dtype=torch.int64, device="cuda")
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    _, out, st = _call(row, t, peers, 0, 2, 50_000_000, status)
+    assert st == 1 and np.isnan(float(out))
+    snap_mine, snap_other = mine.clone(), other.clone()
+    _, out, st = _call(row, t, peers, 0, 2, 50_000_000, status)
+    assert st == 1 and np.isnan(float(out))
+    assert torch.equal(mine, snap_mine) and torch.equal(other, snap_other)
+    assert _lib.lib.b2k_pipeline_timeouts(1) == 1  # only the first call waited
+
+
+def test_peer_flag_ahead_is_an_error():
+    """A peer flag above this rank's epoch (a peer that gave up waiting and
+    stepped on) is reported as status 2, not taken as an arrival."""
+    _lib.lib.b2k_pipeline_timeouts(1)
+    _, t, row = _loss_rows(M=500)
+    nb = int(_lib.lib.b2k_ce_exchange_bytes(2))
+    mine = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+    other = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+    # the first call runs epoch 1 (slot parity 1); rank 1's flag of parity 1
+    # in this rank's buffer sits after the 2 x 2 pairs of 16 B and the three
+    # flags before it: byte 2*2*16 + (1*2 + 1)*8 = 88.  Epoch 3 = two ahead.
+    mine[88:96] = torch.tensor([3], dtype=torch.int64).view(torch.uint8).cuda()
+    peers = torch.tensor([mine.data_ptr(), other.data_ptr()], dtype=torch.int64, device="cuda")
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    _, out, st = _call(row, t, peers, 0, 2, 2_000_000_000, status)
+    assert st == 2 and np.isnan(float(out))
+    assert _lib.lib.b2k_pipeline_timeouts(1) == 1
 
 
 def _free_port():

@@ -6,11 +6,13 @@ binding with device pointers but no allocator): its scratch is a fixed
 buffer inside libb200k.so.  This test calls it through the C ABI, twice in a
 row on different inputs (so stale scratch from the first call cannot leak
 into the second), and compares each result with the allocating path
-(b2k_cross_entropy -> b2k_ce_reduce -> b2k_ce_mean with caller scratch) at
-the cross-entropy tolerance of the other tests (1e-3 relative).  It also
-checks that a row count above the built-in limit is refused before any
-launch.  The file sorts last so a stop-at-first-failure run has already run
-every other test; it needs nothing from them.
+(b2k_cross_entropy -> b2k_ce_reduce -> b2k_ce_mean with caller scratch).
+Both run the same kernels in the same order on the same inputs, so the means
+must be equal bit for bit: a tolerance could hide stale or aliased scratch.
+The row count exactly at the built-in limit is accepted, zero rows give NaN
+(no valid row, as the allocating path), and one row above the limit is
+refused before any launch.  The file sorts last so a stop-at-first-failure
+run has already run every other test; it needs nothing from them.
 """
 import pytest
 import torch
@@ -40,12 +42,27 @@ def _inputs(M, V, seed):
     return x, t
 
 
+def _bits(t):
+    return t.view(torch.int32).item()
+
+
 def test_noalloc_matches_allocating_path_twice():
     for M, V, seed in [(4096, 128256, 1), (777, 32000, 2)]:
         x, t = _inputs(M, V, seed)
-        want = float(b200k.cross_entropy_mean(x, t))
-        got = float(_noalloc(x, t))
-        assert abs(got - want) <= 1e-3 * abs(want), (M, V, got, want)
+        want = b200k.cross_entropy_mean(x, t)
+        got = _noalloc(x, t)
+        assert _bits(got) == _bits(want), (M, V, float(got), float(want))
+
+
+def test_noalloc_at_the_row_limit_and_empty():
+    x, t = _inputs(MAX_ROWS, 64, 3)
+    want = b200k.cross_entropy_mean(x, t)
+    got = _noalloc(x, t)
+    assert _bits(got) == _bits(want), (float(got), float(want))
+    e = torch.empty((0, 64), dtype=torch.bfloat16, device="cuda")
+    te = torch.empty((0,), dtype=torch.int64, device="cuda")
+    assert torch.isnan(_noalloc(e, te)).item()
+    assert torch.isnan(b200k.cross_entropy_mean(e, te)).item()
 
 
 def test_noalloc_rejects_too_many_rows():
