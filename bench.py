@@ -842,6 +842,16 @@ def _eager_table():
         n = rms(x.float()) * w.float()
         return (n * c.float() + rot(n) * s.float()).to(x.dtype)
 
+    def entropy(x):
+        xf = x.float()
+        lse = torch.logsumexp(xf, dim=-1, keepdim=True)
+        return (lse.squeeze(-1) - (xf * torch.exp(xf - lse)).sum(-1)).to(x.dtype)
+
+    def kl_div(x, y):
+        lx = x.float() - torch.logsumexp(x.float(), dim=-1, keepdim=True)
+        ly = y.float() - torch.logsumexp(y.float(), dim=-1, keepdim=True)
+        return (torch.exp(lx) * (lx - ly)).sum(-1).to(x.dtype)
+
     return {  # the expressions of ouroboros/specs.py / chains.py, eager
         "rmsnorm": lambda x, w: rms(x.float()).to(x.dtype) * w,
         "rmsnorm_gemma": lambda x, w: (rms(x.float()) * (1.0 + w.float())).to(x.dtype),
@@ -863,6 +873,10 @@ def _eager_table():
         "rope": lambda x, c, s: (x.float() * c.float() + rot(x.float()) * s.float()).to(x.dtype),
         "rope_interleaved": rope_inter,
         "qknorm_rope": qknorm_rope,
+        "dequant_int8": lambda q, sc: (q.float() * sc.float()).to(torch.float16),
+        "cumsum": lambda x: torch.cumsum(x.float(), dim=-1).to(x.dtype),
+        "entropy": entropy,
+        "kl_div": kl_div,
     }
 
 
@@ -872,7 +886,8 @@ GRID_OPS = {"rmsnorm": "rms", "rmsnorm_gemma": "rms", "softmax": "x", "log_softm
             "gelu": "x", "silu": "x", "add_rmsnorm": "add_rms", "layernorm": "ln",
             "add_layernorm": "add_ln", "layernorm_gelu": "ln", "add_layernorm_gelu": "add_ln",
             "add_rmsnorm_silu": "add_rms", "cross_entropy": "ce", "rope": "rope",
-            "rope_interleaved": "rope_inter", "qknorm_rope": "qkr"}
+            "rope_interleaved": "rope_inter", "qknorm_rope": "qkr", "dequant_int8": "dequant",
+            "cumsum": "x", "entropy": "x", "kl_div": "gate_up"}
 
 
 def _grid_inputs(kind, M, N, dt, device, seed):
@@ -892,6 +907,9 @@ def _grid_inputs(kind, M, N, dt, device, seed):
         return (rn(M, N), rn(M, N))
     if kind == "ce":
         return (rn(M, N), torch.randint(0, N, (M,), generator=g, device=device))
+    if kind == "dequant":
+        q = torch.randint(-128, 128, (M, N), generator=g, device=device, dtype=torch.int8)
+        return (q, (torch.rand((M, 1), generator=g, device=device) * 0.02).to(dt))
     ang = torch.randn((M, N // 2), generator=g, device=device)
     c, s = ang.cos(), ang.sin()
     if kind == "rope_inter":
@@ -952,7 +970,7 @@ def run_grid(args, device):
                 run = b200k.get_op(op)
                 out = run(*probe)
                 e = eager[op]
-                ok, err = _close(out, e(*probe), dt)
+                ok, err = _close(out, e(*probe), out.dtype)
                 nbytes = _algo_bytes(probe, out)
                 nsets = int(max(1, min(64, -(-ROTATE_BYTES // nbytes))))
                 sets = [probe] + [_grid_inputs(kind, M, N, dt, device, 1000 + M + N + 7 * k)

@@ -10,7 +10,7 @@
 // which costs one 32-bit division per vector (rows never straddle a vector
 // because N % E == 0 on this path).  Anything else (odd N, strided rows)
 // takes a scalar grid-stride kernel.
-#include "common.cuh"
+#include "tma.cuh"
 
 namespace b2k {
 
@@ -18,6 +18,24 @@ constexpr int kEwThreads = 256;
 constexpr int kEwUnroll = 4;
 
 // ---------------------------------------------------------------- gated
+// Programmatic dependent launch prologue of the flat vector kernels: let the
+// next kernel of the stream begin launching, give L2 a prefetch hint for this
+// block's 16-byte vectors of each input (they may load while the previous
+// kernel drains), then wait for the previous kernel before reading.
+__device__ __forceinline__ void pdl_prologue_flat(int64_t nvec, int U, const void* a,
+                                                  const void* b) {
+  griddep_launch_dependents();
+  if (threadIdx.x == 0) {
+    const int64_t v0 = (int64_t)blockIdx.x * kEwThreads * U;
+    const int64_t n = nvec - v0 < (int64_t)kEwThreads * U ? nvec - v0 : (int64_t)kEwThreads * U;
+    if (n > 0) {
+      if (a) bulk_prefetch_l2(static_cast<const unsigned char*>(a) + v0 * 16, (uint32_t)(n * 16));
+      if (b) bulk_prefetch_l2(static_cast<const unsigned char*>(b) + v0 * 16, (uint32_t)(n * 16));
+    }
+  }
+  griddep_wait();
+}
+
 template <typename T, int ACT, int U>
 __global__ void __launch_bounds__(kEwThreads) glu_vec_kernel(const T* __restrict__ g,
                                                              const T* __restrict__ u,
@@ -25,6 +43,7 @@ __global__ void __launch_bounds__(kEwThreads) glu_vec_kernel(const T* __restrict
   constexpr int E = Traits<T>::E;
   constexpr bool P = std::is_same<T, float>::value;
   const int64_t base = (int64_t)blockIdx.x * (kEwThreads * U) + threadIdx.x;
+  pdl_prologue_flat(nvec, U, g, u);
   uint4 gv[U], uv[U];
 #pragma unroll
   for (int k = 0; k < U; ++k) {
@@ -69,6 +88,7 @@ __global__ void __launch_bounds__(kEwThreads) act_vec_kernel(const T* __restrict
   constexpr int E = Traits<T>::E;
   constexpr bool P = std::is_same<T, float>::value;
   const int64_t base = (int64_t)blockIdx.x * (kEwThreads * U) + threadIdx.x;
+  pdl_prologue_flat(nvec, U, x, nullptr);
   uint4 xv[U];
 #pragma unroll
   for (int k = 0; k < U; ++k) {
@@ -121,6 +141,7 @@ __global__ void __launch_bounds__(kEwThreads) dequant_vec_kernel(const int8_t* _
                                                                  __half* __restrict__ y,
                                                                  int64_t nvec, uint32_t nvr) {
   const int64_t base = (int64_t)blockIdx.x * (kEwThreads * U) + threadIdx.x;
+  pdl_prologue_flat(nvec, U, q, nullptr);
   uint4 qv[U];
 #pragma unroll
   for (int k = 0; k < U; ++k) {
@@ -171,8 +192,8 @@ static int glu_launch(const void* g, int64_t ldg, const void* u, int64_t ldu, vo
   if (vec) {
     const int64_t nvec = M * N / E;
     const int64_t grid = (nvec + kEwThreads * kEwUnroll - 1) / (kEwThreads * kEwUnroll);
-    glu_vec_kernel<T, ACT, kEwUnroll><<<(unsigned)grid, kEwThreads, 0, st>>>(
-        (const T*)g, (const T*)u, (T*)y, nvec);
+    launch_pdl(glu_vec_kernel<T, ACT, kEwUnroll>, dim3((unsigned)grid), dim3(kEwThreads), 0, st,
+               (const T*)g, (const T*)u, (T*)y, nvec);
   } else {
     glu_scalar_kernel<T, ACT><<<scalar_grid(M * N), kEwThreads, 0, st>>>(
         (const T*)g, ldg, (const T*)u, ldu, (T*)y, ldy, M, N);
@@ -188,11 +209,12 @@ static int act_launch(const void* x, int64_t ldx, const void* bias, void* y, int
     const int64_t nvec = M * N / E;
     const int64_t grid = (nvec + kEwThreads * kEwUnroll - 1) / (kEwThreads * kEwUnroll);
     if (bias)
-      act_vec_kernel<T, ACT, true, kEwUnroll><<<(unsigned)grid, kEwThreads, 0, st>>>(
-          (const T*)x, (const T*)bias, (T*)y, nvec, (uint32_t)(N / E));
+      launch_pdl(act_vec_kernel<T, ACT, true, kEwUnroll>, dim3((unsigned)grid), dim3(kEwThreads),
+                 0, st, (const T*)x, (const T*)bias, (T*)y, nvec, (uint32_t)(N / E));
     else
-      act_vec_kernel<T, ACT, false, kEwUnroll><<<(unsigned)grid, kEwThreads, 0, st>>>(
-          (const T*)x, nullptr, (T*)y, nvec, (uint32_t)(N / E));
+      launch_pdl(act_vec_kernel<T, ACT, false, kEwUnroll>, dim3((unsigned)grid),
+                 dim3(kEwThreads), 0, st, (const T*)x, (const T*)nullptr, (T*)y, nvec,
+                 (uint32_t)(N / E));
   } else {
     act_scalar_kernel<T, ACT><<<scalar_grid(M * N), kEwThreads, 0, st>>>(
         (const T*)x, ldx, (const T*)bias, (T*)y, ldy, M, N);
@@ -271,8 +293,8 @@ extern "C" int b2k_dequant_i8(const void* q, int64_t ldq, const void* scale, int
     if (vec) {
       const int64_t nvec = M * N / 16;
       const int64_t grid = (nvec + kEwThreads * kEwUnroll - 1) / (kEwThreads * kEwUnroll);
-      dequant_vec_kernel<S, kEwUnroll><<<(unsigned)grid, kEwThreads, 0, st>>>(
-          (const int8_t*)q, (const S*)scale, lds, (__half*)y, nvec, (uint32_t)(N / 16));
+      launch_pdl(dequant_vec_kernel<S, kEwUnroll>, dim3((unsigned)grid), dim3(kEwThreads), 0, st,
+                 (const int8_t*)q, (const S*)scale, lds, (__half*)y, nvec, (uint32_t)(N / 16));
     } else {
       dequant_scalar_kernel<S><<<scalar_grid(M * N), kEwThreads, 0, st>>>(
           (const int8_t*)q, ldq, (const S*)scale, lds, (__half*)y, ldy, M, N);

@@ -14,10 +14,10 @@ static int env_int(const char* name, int dflt) {
 // Launch-shape knobs, read once: B2K_NORM_TPR (threads-per-row target of the
 // register path, power of two <= 512), B2K_TMA (0 disables the bulk-copy
 // path), B2K_TMA_THREADS, B2K_TMA_CPS (blocks per SM), B2K_TMA_STAGES,
-// B2K_L2PF_MB (L2 prefetch budget of one bulk-copy launch in MiB, 0 = off).
+// B2K_L2PF_ROWS (rows per block of the bulk-copy path hinted into L2 before
+// the kernel waits for its predecessor; 0 = off).
 struct NormKnobs {
-  int g_target, use_tma, tma_threads, tma_cps, tma_stages;
-  int64_t l2pf;
+  int g_target, use_tma, tma_threads, tma_cps, tma_stages, l2pf;
   NormKnobs() {
     const int t = env_int("B2K_NORM_TPR", 0);
     g_target = (t >= 1 && t <= kNormMaxThreads && (t & (t - 1)) == 0) ? t : 128;
@@ -28,8 +28,7 @@ struct NormKnobs {
     tma_cps = (c >= 1 && c <= 8) ? c : 0;
     const int st = env_int("B2K_TMA_STAGES", 0);
     tma_stages = (st >= 2 && st <= 8) ? st : 0;
-    const int mb = env_int("B2K_L2PF_MB", 32);
-    l2pf = (mb >= 0 && mb <= 96) ? (int64_t)mb << 20 : (int64_t)32 << 20;
+    l2pf = l2_prefetch_rows_knob();
   }
 };
 
@@ -108,7 +107,7 @@ extern "C" int b2k_norm(const void* x, int64_t ldx, const void* r, int64_t ldr, 
   a.tma_threads = kn.tma_threads;
   a.tma_cps = kn.tma_cps;
   a.tma_stages = kn.tma_stages;
-  a.l2_prefetch_bytes = kn.l2pf;
+  a.l2_prefetch_rows = kn.l2pf;
   const int es = dtype_size(dtype);
   const int E = es ? 16 / es : 1;
   bool al = (N % E == 0) && aligned16(x) && aligned16(y) && ((ldx * es) % 16 == 0) &&

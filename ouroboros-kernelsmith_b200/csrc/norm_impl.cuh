@@ -54,7 +54,7 @@ struct NormArgs {
   int tma_cps;     // CTAs per SM of the bulk-copy path (0 = automatic)
   int tma_stages;  // pipeline depth (0 = automatic)
   int use_tma;     // 0 disables the bulk-copy path
-  int64_t l2_prefetch_bytes;  // bulk-copy path: L2 prefetch budget of one launch (0 = off)
+  int l2_prefetch_rows;  // bulk-copy path: rows per block hinted into L2 before the wait
 };
 
 constexpr int kNormMaxThreads = 512;
@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
   const void* srcs[2] = {a.x, a.r};
   const int64_t lds[2] = {a.ldx, a.ldr};
   RowPipe<NIN>::prefetch_l2(srcs, lds, (int)sizeof(T), (uint32_t)N * (uint32_t)sizeof(T), a.M,
-                            a.l2_prefetch_bytes);
+                            a.l2_prefetch_rows);
   griddep_wait();  // inputs may come from the previous kernel in the stream
   RowPipe<NIN> pipe;
   pipe.init(dsm, S, a.M, (uint32_t)N * (uint32_t)sizeof(T), srcs, lds, (int)sizeof(T));

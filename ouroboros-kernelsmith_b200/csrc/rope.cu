@@ -11,6 +11,7 @@
 // b2k_norm_rope: RMSNorm over the head dim in registers, the normalised row
 // staged in shared memory so each element can read its rotation partner.
 #include "rowio.cuh"
+#include "tma.cuh"
 
 namespace b2k {
 
@@ -149,6 +150,23 @@ __global__ void __launch_bounds__(1024) rope_qk_kernel(const RopeQkArgs a) {
   const int D = a.D, half = D / 2;
   const int heads = (int)(a.H + a.Hk);
   const int c = threadIdx.x * E;
+  // programmatic dependent launch: the next kernel may begin launching; L2
+  // prefetch hints for this block's q and k rows (contiguous per position)
+  // while the previous kernel drains; then wait for it before reading
+  griddep_launch_dependents();
+  if (threadIdx.x == 0 && threadIdx.y == 0) {
+#pragma unroll
+    for (int u = 0; u < kRopePos; ++u) {
+      const int64_t p = p0 + u;
+      if (p < npos) {
+        if (a.H) bulk_prefetch_l2(static_cast<const T*>(a.q) + p * a.H * D,
+                                  (uint32_t)(a.H * D * (int64_t)sizeof(T)));
+        if (a.Hk) bulk_prefetch_l2(static_cast<const T*>(a.k) + p * a.Hk * D,
+                                   (uint32_t)(a.Hk * D * (int64_t)sizeof(T)));
+      }
+    }
+  }
+  griddep_wait();
   for (int hh = threadIdx.y; hh < heads; hh += blockDim.y) {
     const bool isq = hh < a.H;
     const int64_t hstride = isq ? a.H * D : a.Hk * D;  // elements per position
@@ -534,12 +552,9 @@ extern "C" int b2k_rope_qk(const void* q, const void* k, const void* cos, const 
         return s ? atoi(s) : 1;
       }();
       const bool adj = use_adj && aligned16(cos) && aligned16(sin) && ((D / 2) * es) % 16 == 0;
-      if (interleaved && adj)
-        rope_qk_kernel<T, 2><<<(unsigned)grid, block, 0, st>>>(a);
-      else if (interleaved)
-        rope_qk_kernel<T, 1><<<(unsigned)grid, block, 0, st>>>(a);
-      else
-        rope_qk_kernel<T, 0><<<(unsigned)grid, block, 0, st>>>(a);
+      auto kern = interleaved ? (adj ? rope_qk_kernel<T, 2> : rope_qk_kernel<T, 1>)
+                              : rope_qk_kernel<T, 0>;
+      launch_pdl(kern, dim3((unsigned)grid), block, 0, st, a);
     } else {
       const int64_t items = B * S * (H + Hk) * (D / 2);
       if (interleaved)

@@ -28,6 +28,7 @@ struct SoftmaxArgs {
   const void* scale;
   int scale_dtype;
   int aligned;
+  int l2pf_rows;  // bulk-copy path: rows per block hinted into L2 before the wait
 };
 
 __device__ __forceinline__ float load_scalar(const void* p, int dtype) {
@@ -174,11 +175,17 @@ __global__ void __launch_bounds__(kSmMaxThreads) softmax_tma_kernel(const Softma
   __shared__ volatile int abort_flag;
   const Group g;
   const int N = a.N;
-  const float scale = (KIND == B2K_SOFTMAX_SCALE) ? load_scalar(a.scale, a.scale_dtype) : 1.0f;
   if (g.tx == 0) abort_flag = 0;
-  RowPipe<1> pipe;
+  // programmatic dependent launch: first row hinted into L2, then wait for
+  // the previous kernel before any read
+  griddep_launch_dependents();
   const void* srcs[1] = {a.x};
   const int64_t lds[1] = {a.ldx};
+  RowPipe<1>::prefetch_l2(srcs, lds, (int)sizeof(T), (uint32_t)N * (uint32_t)sizeof(T), a.M,
+                          a.l2pf_rows);
+  griddep_wait();
+  const float scale = (KIND == B2K_SOFTMAX_SCALE) ? load_scalar(a.scale, a.scale_dtype) : 1.0f;
+  RowPipe<1> pipe;
   pipe.init(dsm, S_, a.M, (uint32_t)N * (uint32_t)sizeof(T), srcs, lds, (int)sizeof(T));
   int64_t k = 0;
   for (; k < pipe.nrows; ++k) {
@@ -289,7 +296,7 @@ static int softmax_launch(const SoftmaxArgs& a, cudaStream_t st) {
         const size_t smem = RowPipe<1>::smem_bytes(ps.S, row_bytes);
         int64_t grid = (int64_t)sm_count() * ps.cps;
         if (grid > a.M) grid = a.M;
-        kern<<<(unsigned)grid, G, smem, st>>>(a, ps.S);
+        launch_pdl(kern, dim3((unsigned)grid), dim3(G), smem, st, a, ps.S);
         return check_launch("b2k_softmax(tma)");
       }
     }
@@ -327,6 +334,7 @@ extern "C" int b2k_softmax(const void* x, int64_t ldx, void* y, int64_t ldy, int
   SoftmaxArgs a;
   a.x = x; a.y = y; a.ldx = ldx; a.ldy = ldy; a.M = M; a.N = (int)N;
   a.scale = scale; a.scale_dtype = scale_dtype;
+  a.l2pf_rows = l2_prefetch_rows_knob();
   const int es = dtype_size(dtype);
   const int E = es ? 16 / es : 1;
   a.aligned = (N % E == 0) && aligned16(x) && aligned16(y) && ((ldx * es) % 16 == 0) &&

@@ -7,6 +7,8 @@
 // (read on the host with b2k_pipeline_timeouts) and leaves the loop.
 #pragma once
 
+#include <stdlib.h>
+
 #include "common.cuh"
 
 namespace b2k {
@@ -120,6 +122,64 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// ---------------------------------------------------------------------------
+// Thread-block cluster primitives (distributed shared memory between the
+// CTAs of one cluster on this GPU; no multicast).
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+// all threads of every CTA of the cluster (release / acquire at cluster scope)
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+// shared::cluster address of the same variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32x4(uint32_t addr, float a, float b, float c,
+                                                 float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+// arrive on an mbarrier of another CTA of the cluster; release at cluster
+// scope orders this thread's earlier st.shared::cluster before the arrival
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// bounded wait on a local mbarrier whose arrivals come from other CTAs of the
+// cluster (acquire at cluster scope: their stores before the arrival are seen)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  unsigned long long limit_ns = kTimeoutNs) {
+  if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer() - t0 > limit_ns) return false;
+  }
+}
+
 // Programmatic dependent launch: the kernel may start while the previous
 // kernel in the stream is still finishing; every input read must come after
 // griddep_wait(), which returns once the preceding grid has completed and its
@@ -131,6 +191,34 @@ __device__ __forceinline__ void griddep_wait() {
 }
 __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch with programmatic dependent launch enabled (B2K_PDL=0 disables it):
+// the kernel's blocks may be scheduled while the previous kernel of the
+// stream drains; the kernel itself calls griddep_wait() before its first
+// global read.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* s = getenv("B2K_PDL");
+    return !(s && s[0] == '0');
+  }();
+  return on;
+}
+
+template <typename Kernel, typename... Args>
+inline void launch_pdl(Kernel kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 // Host-side registry of per-translation-unit timeout counters.

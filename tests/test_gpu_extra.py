@@ -278,3 +278,42 @@ def test_two_devices_in_one_process():
         torch.cuda.synchronize(d)
         ok, err, bad = allclose_report(y.cpu().numpy(), ref, *tol_for("rmsnorm", "f32"))
         assert ok, f"cuda:{d}: max err {err}, {bad} bad"
+
+
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("M", [3, 700, 2000, 8000])
+def test_cross_entropy_rows_shared_by_a_cluster(dt, M):
+    """Long rows with few rows per resident block (a vocabulary-sized shard
+    on one of many GPUs): each row is split over the CTAs of a cluster, 4 per
+    row below 12 rows per block, 2 below 24, and the (max, sum-exp) pairs
+    meet in distributed shared memory.  Sampled rows against the oracle,
+    including ignored rows, a bad target (NaN) and targets in the first and
+    last chunk of a row, plus the mean over all rows."""
+    V = 128256
+    g = torch.Generator(device="cuda").manual_seed(M)
+    x = (torch.randn((M, V), generator=g, device="cuda") * 3).to(TDT[dt])
+    t = torch.randint(0, V, (M,), generator=g, device="cuda")
+    t[::17] = -100
+    t[0] = 0
+    if M > 2:
+        t[1] = V - 1
+        t[2] = V + 5  # outside [0, V): NaN
+    out = b200k.cross_entropy(x, t)
+    rows = np.unique(np.concatenate([[0, 1, M - 1], np.arange(0, M, max(1, M // 13))]))
+    rows = rows[rows != 2] if M > 2 else rows
+    xs = x[rows].float().cpu().numpy()
+    ts = t[rows].cpu().numpy()
+    ref = O.cross_entropy(xs, ts, dt)
+    _close(out[rows], ref, dt)
+    if M > 2:
+        assert torch.isnan(out[2]).item()
+        keep = torch.ones(M, dtype=torch.bool, device="cuda")
+        keep[2] = False
+        x, t = x[keep], t[keep]
+    got = float(b200k.cross_entropy_mean(x, t))
+    s, c = 0.0, 0
+    for r in range(0, x.shape[0], 1024):
+        s += float(torch.nn.functional.cross_entropy(x[r:r + 1024].float(), t[r:r + 1024],
+                                                     ignore_index=-100, reduction="sum"))
+        c += int((t[r:r + 1024] != -100).sum())
+    assert abs(got - s / c) <= 1e-3 * abs(s / c), (got, s / c)
