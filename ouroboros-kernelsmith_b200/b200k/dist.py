@@ -142,6 +142,8 @@ class CeExchange:
         completed (no host synchronisation)."""
         if self.failed:
             self._raise(self.failed)
+        if torch.cuda.is_current_stream_capturing():
+            return  # no event query inside a stream capture
         if self.status_event.query():
             v = int(self.status_host[0])
             if v:
