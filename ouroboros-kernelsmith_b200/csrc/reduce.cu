@@ -10,7 +10,12 @@
 // E contiguous elements, the group scans the thread totals, and a running
 // carry joins the chunks.  Accumulation is in fp64 (torch's CPU cumsum of
 // float accumulates in double), output rounded once to fp32 and then to T.
+#include <stdlib.h>
+
 #include "rowio.cuh"
+#include "rowpipe.cuh"
+
+B2K_DEFINE_TIMEOUT_COUNTER()
 
 namespace b2k {
 
@@ -23,6 +28,7 @@ struct RowRedArgs {
   int64_t ldx, ldy, ldo, M;
   int N;
   int aligned;
+  int l2pf_rows;  // pipelined path: rows per block hinted into L2 before the wait
 };
 
 // ---------------------------------------------------------------- entropy
@@ -257,9 +263,375 @@ __global__ void __launch_bounds__(kRedMaxThreads) cumsum_kernel(const RowRedArgs
   }
 }
 
+// ---------------------------------------------------------------- pipelined path
+// Aligned rows whose inputs fit a ring stage (<= 64 KB): persistent blocks
+// walk their rows through the bulk-copy row pipeline (rowpipe.cuh), one row
+// per block at a time, the next one streaming in while the current one is
+// reduced.  The row is read once; every pass of the reference runs over
+// registers, and each row costs ONE block-wide merge:
+//  * entropy: per thread (m, s, t) = (max, sum e^(x-m), sum x e^(x-m)) over its
+//    slice, merged across the block like a logsumexp.  Then lse = M + log S
+//    and sum x exp(x - lse) = T * exp(M - lse): the reference's p = exp(x -
+//    lse) factored through the same rounded lse, so the cancellation of lse
+//    against the weighted sum that decides peaked rows is the reference's,
+//    with one exponential per element instead of two.
+//  * kl_div: (mx, sx, u) with u = sum e^(x-mx) (x - y), and (my, sy).  With
+//    w = exp(Mx - lse_x): sum exp(lx)(lx - ly) = w U - (lse_x - lse_y) Sx w,
+//    two exponentials per element instead of three.
+//  * cumsum: each thread takes a contiguous run of the row, prefix-sums it in
+//    fp32, and the block scans the per-thread totals in fp64; an output is
+//    the thread's fp64 offset (rounded once to fp32) plus its local prefix.
+
+// merge of K floats across the block (one row per block), every thread gets
+// the result; red holds K * 32 floats
+template <int K, typename Merge>
+__device__ __forceinline__ void block_merge(float (&v)[K], const float (&ident)[K], float* red,
+                                            Merge merge) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float u[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) u[k] = __shfl_xor_sync(0xffffffffu, v[k], o);
+    merge(v, u);
+  }
+  if (nw > 1) {
+    if (lane == 0)
+#pragma unroll
+      for (int k = 0; k < K; ++k) red[k * 32 + w] = v[k];
+    __syncthreads();
+    if (w == 0) {
+#pragma unroll
+      for (int k = 0; k < K; ++k) v[k] = lane < nw ? red[k * 32 + lane] : ident[k];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        float u[K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) u[k] = __shfl_xor_sync(0xffffffffu, v[k], o);
+        merge(v, u);
+      }
+      if (lane == 0)
+#pragma unroll
+        for (int k = 0; k < K; ++k) red[k * 32] = v[k];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < K; ++k) v[k] = red[k * 32];
+    __syncthreads();  // red is reused by the next row
+  }
+}
+
+template <bool P>
+__device__ __forceinline__ float exp_of(float x) {
+  if constexpr (P) return expf(x);
+  else return ex2_approx(x * kLog2e);
+}
+
+// (m, s, t...) logsumexp-style merge: the values after the max are sums
+// scaled by e^(x - m)
+template <bool P, int K>
+__device__ __forceinline__ void lse_merge_k(float (&a)[K], const float (&b)[K]) {
+  const float M = fmaxf(a[0], b[0]);
+  if (M == -INFINITY) return;
+  const float fa = exp_of<P>(a[0] - M), fb = exp_of<P>(b[0] - M);
+#pragma unroll
+  for (int k = 1; k < K; ++k) a[k] = a[k] * fa + b[k] * fb;
+  a[0] = M;
+}
+
+// sum of e^(x - m) (and of x e^(x - m) / e^(x - m) (x - y)) over a slice, one
+// exponential per element; f32x2 + ex2.approx for 16-bit inputs
+template <typename T, int V>
+struct RedSlice {
+  static constexpr int E = Traits<T>::E;
+  static constexpr int H = E / 2;
+  static constexpr bool P = std::is_same<T, float>::value;
+
+  __device__ __forceinline__ static float vmax(const float2 (&x)[V][H], const bool (&in)[V]) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+      if (in[v])
+#pragma unroll
+        for (int j = 0; j < H; ++j) m = fmaxf(m, fmaxf(x[v][j].x, x[v][j].y));
+    return m;
+  }
+  // s += e^(x-m); t += x e^(x-m) (y == nullptr) or e^(x-m) (x - y)
+  __device__ __forceinline__ static void sums(const float2 (&x)[V][H], const float2 (*y)[H],
+                                              const bool (&in)[V], float m, float& s, float& t) {
+    s = 0.0f;
+    t = 0.0f;
+    if (m == -INFINITY) return;
+    float2 s2 = f2s(0.0f), t2 = f2s(0.0f);
+    const float2 nz = f2s(-m * kLog2e);
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+      if (in[v])
+#pragma unroll
+        for (int j = 0; j < H; ++j) {
+          float2 e;
+          if constexpr (P) {
+            e = f2(expf(x[v][j].x - m), expf(x[v][j].y - m));
+          } else {
+            const float2 z = fma2(x[v][j], f2s(kLog2e), nz);
+            e = f2(ex2_approx(z.x), ex2_approx(z.y));
+          }
+          s2 = add2(s2, e);
+          const float2 wgt = y ? sub2(x[v][j], y[v][j]) : x[v][j];
+          t2 = fma2(wgt, e, t2);
+        }
+    s = s2.x + s2.y;
+    t = t2.x + t2.y;
+  }
+};
+
+template <typename T, int V>
+__global__ void __launch_bounds__(kRedMaxThreads) entropy_tma_kernel(const RowRedArgs a,
+                                                                    const int S_) {
+  constexpr int E = Traits<T>::E;
+  constexpr int H = E / 2;
+  constexpr bool P = std::is_same<T, float>::value;
+  using Sl = RedSlice<T, V>;
+  extern __shared__ __align__(128) unsigned char dsm[];
+  __shared__ float red[3 * 32];
+  __shared__ volatile int abort_flag;
+  const int G = blockDim.x, tx = threadIdx.x;
+  const int N = a.N;
+  if (tx == 0) abort_flag = 0;
+  griddep_launch_dependents();
+  const void* srcs[1] = {a.x};
+  const int64_t lds[1] = {a.ldx};
+  RowPipe<1>::prefetch_l2(srcs, lds, (int)sizeof(T), (uint32_t)N * (uint32_t)sizeof(T), a.M,
+                          a.l2pf_rows);
+  griddep_wait();
+  RowPipe<1> pipe;
+  pipe.init(dsm, S_, a.M, (uint32_t)N * (uint32_t)sizeof(T), srcs, lds, (int)sizeof(T));
+  const float ident[3] = {-INFINITY, 0.0f, 0.0f};
+  int64_t k = 0;
+  for (; k < pipe.nrows; ++k) {
+    bool ok;
+    const T* xs = reinterpret_cast<const T*>(pipe.wait_next(ok));
+    if (!ok) { abort_flag = 1; atomicAdd(&b2k_tu_timeouts, 1u); }
+    float2 xv[V][H];
+    bool in[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * G + tx) * E;
+      in[v] = c < N;
+      if (in[v]) unpack2<T>(*reinterpret_cast<const uint4*>(xs + c), xv[v]);
+      else
+#pragma unroll
+        for (int j = 0; j < H; ++j) xv[v][j] = f2s(0.0f);
+    }
+    float r[3];
+    r[0] = Sl::vmax(xv, in);
+    Sl::sums(xv, nullptr, in, r[0], r[1], r[2]);
+    block_merge<3>(r, ident, red, [](float (&p)[3], const float (&q)[3]) {
+      lse_merge_k<P, 3>(p, q);
+    });  // barriers inside: every thread has read the stage
+    if (abort_flag) break;
+    pipe.refill();
+    if (tx == 0) {
+      const float lse = r[0] + (P ? logf(r[1]) : f_log<false>(r[1]));
+      const float q = r[2] * exp_of<P>(r[0] - lse);
+      static_cast<T*>(a.out)[pipe.row_of(k) * a.ldo] = from_f<T>(lse - q);
+    }
+  }
+  pipe.drain(k);
+}
+
+template <typename T, int V>
+__global__ void __launch_bounds__(kRedMaxThreads) kl_tma_kernel(const RowRedArgs a, const int S_) {
+  constexpr int E = Traits<T>::E;
+  constexpr int H = E / 2;
+  constexpr bool P = std::is_same<T, float>::value;
+  using Sl = RedSlice<T, V>;
+  extern __shared__ __align__(128) unsigned char dsm[];
+  __shared__ float red[5 * 32];
+  __shared__ volatile int abort_flag;
+  const int G = blockDim.x, tx = threadIdx.x;
+  const int N = a.N;
+  if (tx == 0) abort_flag = 0;
+  griddep_launch_dependents();
+  const void* srcs[2] = {a.x, a.y};
+  const int64_t lds[2] = {a.ldx, a.ldy};
+  RowPipe<2>::prefetch_l2(srcs, lds, (int)sizeof(T), (uint32_t)N * (uint32_t)sizeof(T), a.M,
+                          a.l2pf_rows);
+  griddep_wait();
+  RowPipe<2> pipe;
+  pipe.init(dsm, S_, a.M, (uint32_t)N * (uint32_t)sizeof(T), srcs, lds, (int)sizeof(T));
+  const float ident[5] = {-INFINITY, 0.0f, 0.0f, -INFINITY, 0.0f};
+  auto merge5 = [](float (&p)[5], const float (&q)[5]) {
+    float a3[3] = {p[0], p[1], p[2]}, b3[3] = {q[0], q[1], q[2]};
+    lse_merge_k<P, 3>(a3, b3);
+    float a2[2] = {p[3], p[4]}, b2[2] = {q[3], q[4]};
+    lse_merge_k<P, 2>(a2, b2);
+    p[0] = a3[0]; p[1] = a3[1]; p[2] = a3[2]; p[3] = a2[0]; p[4] = a2[1];
+  };
+  int64_t k = 0;
+  for (; k < pipe.nrows; ++k) {
+    bool ok;
+    const T* xs = reinterpret_cast<const T*>(pipe.wait_next(ok));
+    if (!ok) { abort_flag = 1; atomicAdd(&b2k_tu_timeouts, 1u); }
+    const T* ys = xs + N;
+    float2 xv[V][H], yv[V][H];
+    bool in[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * G + tx) * E;
+      in[v] = c < N;
+      if (in[v]) {
+        unpack2<T>(*reinterpret_cast<const uint4*>(xs + c), xv[v]);
+        unpack2<T>(*reinterpret_cast<const uint4*>(ys + c), yv[v]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < H; ++j) { xv[v][j] = f2s(0.0f); yv[v][j] = f2s(0.0f); }
+      }
+    }
+    float r[5];
+    r[0] = Sl::vmax(xv, in);
+    Sl::sums(xv, yv, in, r[0], r[1], r[2]);
+    r[3] = Sl::vmax(yv, in);
+    float unused;
+    Sl::sums(yv, nullptr, in, r[3], r[4], unused);
+    block_merge<5>(r, ident, red, merge5);
+    if (abort_flag) break;
+    pipe.refill();
+    if (tx == 0) {
+      const float lsex = r[0] + (P ? logf(r[1]) : f_log<false>(r[1]));
+      const float lsey = r[3] + (P ? logf(r[4]) : f_log<false>(r[4]));
+      const float w = exp_of<P>(r[0] - lsex);
+      static_cast<T*>(a.out)[pipe.row_of(k) * a.ldo] =
+          from_f<T>(w * r[2] - (lsex - lsey) * (r[1] * w));
+    }
+  }
+  pipe.drain(k);
+}
+
+// inclusive scan of one double per thread across the block (one row per
+// block); sred holds 32 doubles
+__device__ __forceinline__ double block_scan_incl(double v, double* sred) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double u = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += u;
+  }
+  if (nw > 1) {
+    if (lane == 31) sred[w] = v;
+    __syncthreads();
+    if (w == 0) {
+      double t = lane < nw ? sred[lane] : 0.0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double u = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += u;
+      }
+      if (lane < nw) sred[lane] = t;  // inclusive totals of warps 0..lane
+    }
+    __syncthreads();
+    if (w > 0) v += sred[w - 1];
+    __syncthreads();  // sred is reused by the next row
+  }
+  return v;
+}
+
+template <typename T, int V>
+__global__ void __launch_bounds__(kRedMaxThreads) cumsum_tma_kernel(const RowRedArgs a,
+                                                                   const int S_) {
+  constexpr int E = Traits<T>::E;
+  extern __shared__ __align__(128) unsigned char dsm[];
+  __shared__ double sred[32];
+  __shared__ volatile int abort_flag;
+  const int tx = threadIdx.x;
+  const int N = a.N;
+  if (tx == 0) abort_flag = 0;
+  griddep_launch_dependents();
+  const void* srcs[1] = {a.x};
+  const int64_t lds[1] = {a.ldx};
+  RowPipe<1>::prefetch_l2(srcs, lds, (int)sizeof(T), (uint32_t)N * (uint32_t)sizeof(T), a.M,
+                          a.l2pf_rows);
+  griddep_wait();
+  RowPipe<1> pipe;
+  pipe.init(dsm, S_, a.M, (uint32_t)N * (uint32_t)sizeof(T), srcs, lds, (int)sizeof(T));
+  int64_t k = 0;
+  for (; k < pipe.nrows; ++k) {
+    bool ok;
+    const T* xs = reinterpret_cast<const T*>(pipe.wait_next(ok));
+    if (!ok) { abort_flag = 1; atomicAdd(&b2k_tu_timeouts, 1u); }
+    // this thread's contiguous run: vectors tx*V .. tx*V + V - 1
+    float f[V][E];
+    float run = 0.0f;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (tx * V + v) * E;
+      if (c < N) unpack<T>(*reinterpret_cast<const uint4*>(xs + c), f[v]);
+      else
+#pragma unroll
+        for (int e = 0; e < E; ++e) f[v][e] = 0.0f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) { run += f[v][e]; f[v][e] = run; }
+    }
+    const double incl = block_scan_incl((double)run, sred);  // barriers: the stage was read
+    if (abort_flag) break;
+    pipe.refill();
+    const float base = (float)(incl - (double)run);
+    T* yr = static_cast<T*>(a.out) + pipe.row_of(k) * a.ldo;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (tx * V + v) * E;
+      if (c < N) {
+        float o[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[e] = base + f[v][e];
+        st_stream(yr + c, pack<T>(o));
+      }
+    }
+  }
+  pipe.drain(k);
+}
+
+// The pipelined kernels, when the rows are aligned and a ring stage (all
+// inputs of one row) is at most 64 KB: kind 0 entropy, 1 kl_div, 2 cumsum.
+// Threads per row: two 16-byte vectors each while that fits 512 threads.
+template <typename T>
+static bool rowred_try_tma(const RowRedArgs& a, int kind, cudaStream_t st) {
+  constexpr int E = Traits<T>::E;
+  static const int use_tma = [] {
+    const char* s = getenv("B2K_TMA");
+    return s ? atoi(s) : 1;
+  }();
+  if (!use_tma || !a.aligned) return false;
+  const int64_t nvec = a.N / E;
+  const int nin = kind == 1 ? 2 : 1;
+  const int64_t row_bytes = (int64_t)a.N * (int64_t)sizeof(T);
+  if (nvec < 64 || nin * row_bytes > (64 << 10)) return false;
+  int G = next_pow2((nvec + 1) / 2);
+  G = G < 64 ? 64 : (G > kRedMaxThreads ? kRedMaxThreads : G);
+  const int64_t vneed = (nvec + G - 1) / G;
+  if (vneed > 4) return false;
+  const bool v2 = vneed <= 2;
+  auto go = [&](auto kern, int n_in) -> bool {
+    PipeShape ps;
+    if (!choose_pipe_shape(kern, G, n_in * row_bytes, 0, 2, &ps)) return false;
+    const size_t smem = (size_t)ps.S * n_in * (size_t)row_bytes + (size_t)ps.S * sizeof(uint64_t);
+    int64_t grid = (int64_t)sm_count() * ps.cps;
+    if (grid > a.M) grid = a.M;
+    const int64_t per = (a.M + grid - 1) / grid;  // every block walks the same number of rows
+    grid = (a.M + per - 1) / per;
+    launch_pdl(kern, dim3((unsigned)grid), dim3(G), smem, st, a, ps.S);
+    return true;
+  };
+  if (kind == 0) return go(v2 ? entropy_tma_kernel<T, 2> : entropy_tma_kernel<T, 4>, 1);
+  if (kind == 1) return go(v2 ? kl_tma_kernel<T, 2> : kl_tma_kernel<T, 4>, 2);
+  return go(v2 ? cumsum_tma_kernel<T, 2> : cumsum_tma_kernel<T, 4>, 1);
+}
+
 template <typename T>
 static int rowred_launch(const RowRedArgs& a, bool kl, cudaStream_t st) {
   constexpr int E = Traits<T>::E;
+  if (rowred_try_tma<T>(a, kl ? 1 : 0, st))
+    return check_launch(kl ? "b2k_kl_div(tma)" : "b2k_entropy(tma)");
   RowCfg cfg;
   if (choose_row_cfg(a.N, E, 128, &cfg, 4, kRedMaxThreads)) {
     const dim3 block(cfg.G, cfg.R);
@@ -288,6 +660,7 @@ static int rowred_launch(const RowRedArgs& a, bool kl, cudaStream_t st) {
 template <typename T>
 static int cumsum_launch(const RowRedArgs& a, cudaStream_t st) {
   constexpr int E = Traits<T>::E;
+  if (rowred_try_tma<T>(a, 2, st)) return check_launch("b2k_cumsum(tma)");
   const int64_t nvec = (a.N + E - 1) / E;
   int G = next_pow2(nvec);
   G = G < 1 ? 1 : (G > 256 ? 256 : G);
@@ -318,6 +691,7 @@ extern "C" int b2k_entropy(const void* x, int64_t ldx, void* out, int64_t M, int
   RowRedArgs a;
   a.x = x; a.y = nullptr; a.out = out; a.ldx = ldx; a.ldy = 0; a.ldo = 1; a.M = M; a.N = (int)N;
   a.aligned = rows_aligned(x, ldx, nullptr, 0, N, dtype_size(dtype));
+  a.l2pf_rows = l2_prefetch_rows_knob();
   B2K_DISPATCH_FLOAT(dtype, { return rowred_launch<T>(a, false, (cudaStream_t)stream); });
   return B2K_OK;
 }
@@ -331,6 +705,7 @@ extern "C" int b2k_kl_div(const void* x, int64_t ldx, const void* y, int64_t ldy
   RowRedArgs a;
   a.x = x; a.y = y; a.out = out; a.ldx = ldx; a.ldy = ldy; a.ldo = 1; a.M = M; a.N = (int)N;
   a.aligned = rows_aligned(x, ldx, y, ldy, N, dtype_size(dtype));
+  a.l2pf_rows = l2_prefetch_rows_knob();
   B2K_DISPATCH_FLOAT(dtype, { return rowred_launch<T>(a, true, (cudaStream_t)stream); });
   return B2K_OK;
 }
@@ -344,6 +719,7 @@ extern "C" int b2k_cumsum(const void* x, int64_t ldx, void* y, int64_t ldy, int6
   RowRedArgs a;
   a.x = x; a.y = nullptr; a.out = y; a.ldx = ldx; a.ldy = 0; a.ldo = ldy; a.M = M; a.N = (int)N;
   a.aligned = rows_aligned(x, ldx, y, ldy, N, dtype_size(dtype));
+  a.l2pf_rows = l2_prefetch_rows_knob();
   B2K_DISPATCH_FLOAT(dtype, { return cumsum_launch<T>(a, (cudaStream_t)stream); });
   return B2K_OK;
 }

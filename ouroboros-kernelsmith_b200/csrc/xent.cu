@@ -17,8 +17,6 @@
 // b2k_ce_mean turns the (possibly all-reduced) pair into the mean.
 #include <stdlib.h>
 
-#include <mutex>
-
 #include "rowio.cuh"
 #include "rowpipe.cuh"
 #include "tma.cuh"
@@ -459,297 +457,6 @@ __global__ void __launch_bounds__(kCeThreads) ce_tma_kernel(const CeArgs a, cons
       mbar_wait(&full[(int)(j % S)], (uint32_t)((j / S) & 1));
 }
 
-// Few rows per block (a large vocabulary whose rows are split over many GPUs:
-// 4096 rows of 128256 at 8 GPUs are 9.2 rows per resident block, so the last
-// round of rows would run on a fraction of the blocks): each row is shared by
-// the P CTAs of a thread-block cluster.  CTA j of the cluster streams chunks
-// [j*nchunks/P, (j+1)*nchunks/P) of every row of the cluster through its own
-// ring (the producer / consumer scheme of ce_tma_kernel) and reduces them to
-// a (max, sum-exp) pair, plus the target logit when its chunk is in the
-// slice.  The pairs meet in CTA 0's shared memory: CTA j stores its pair into
-// CTA 0's slot for the row (distributed shared memory) and arrives on CTA 0's
-// merge barrier.  CTA 0 merges row i at the end of row i+1, so it never waits
-// for slices still in progress, then frees the slot with an arrival on each
-// CTA's slot_free barrier; slots alternate by the parity of the merged-row
-// counter, so a CTA waits for slot_free only when it is two rows ahead of CTA
-// 0.  Every wait is bounded; a CTA stops at the next row after a timeout.  The
-// CTAs of a cluster see the same targets, so they skip the same ignored rows
-// and agree on the counter.
-constexpr int kCeMaxSplit = 8;
-
-template <typename T, typename OutT>
-__global__ void __launch_bounds__(kCeThreads, 3) ce_split_kernel(const CeArgs a, const int S) {
-  constexpr int E = Traits<T>::E;
-  constexpr int H = E / 2;
-  constexpr bool P32 = std::is_same<T, float>::value;
-  constexpr int NC = 32 * kCeConsumerWarps;
-  constexpr int CE = kCeChunkBytes / (int)sizeof(T);
-  constexpr int VPT = CE / E / NC;
-  static_assert(VPT * E * NC == CE, "chunk must split evenly over the consumers");
-  extern __shared__ __align__(128) unsigned char dsm[];
-  __shared__ float red_m[kCeConsumerWarps], red_s[kCeConsumerWarps];
-  __shared__ volatile int abort_flag;
-  __shared__ int stop;
-  __shared__ float xt_s;
-  __shared__ int64_t consumed;
-  __shared__ __align__(16) float4 slot[2][kCeMaxSplit];  // used in CTA 0
-  __shared__ __align__(8) uint64_t merge_full[2];         // CTA 0: P-1 arrivals a phase
-  __shared__ __align__(8) uint64_t slot_free[2];          // CTA j > 0: one arrival a phase
-  // CTA 0's row whose merge is pending (merged at the end of the next row)
-  __shared__ float4 pend_v_s;
-  __shared__ int64_t pend_row_s;
-  __shared__ uint32_t pend_nm_s;
-  __shared__ int pend_s;
-  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + (size_t)S * kCeChunkBytes);
-  uint64_t* empty = full + S;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t P = cluster_nctarank(), rank = cluster_ctarank();
-  const int64_t cid = blockIdx.x / P, ncl = gridDim.x / P;
-  const int64_t nrows = cid < a.M ? (a.M - 1 - cid) / ncl + 1 : 0;
-  const int64_t N = a.N;
-  const int64_t nchunks = (N + CE - 1) / CE;
-  const int64_t c0 = (int64_t)rank * nchunks / P, c1 = ((int64_t)rank + 1) * nchunks / P;
-  const T* xg = static_cast<const T*>(a.x);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kCeConsumerWarps);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&merge_full[s], P - 1);
-      mbar_init(&slot_free[s], 1);
-    }
-    fence_barrier_init();
-    abort_flag = 0;
-    stop = 0;
-    consumed = 0;
-    pend_s = 0;
-  }
-  // every CTA's barriers exist before any CTA of the cluster arrives remotely
-  cluster_sync_all();
-
-  int64_t issued = 0;
-  int p_stage = 0;
-  uint32_t p_phase = 0;
-  if (warp == 0) {
-    // ---- producer warp: this CTA's slice of every row of the cluster
-    for (int64_t i = 0; i < nrows; ++i) {
-      if (__any_sync(0xffffffffu, abort_flag != 0)) break;
-      const int64_t row = cid + i * ncl;
-      const int64_t t = a.tgt[row];
-      if (t == a.ignore || t < 0 || t >= N) continue;
-      const T* xr = xg + row * a.ldx;
-      bool ok = true;
-      for (int64_t c = c0; c < c1; ++c) {
-        const int s = p_stage;
-        if (issued >= S) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], p_phase ^ 1u));
-          if (!ok) {
-            if (lane == 0) { abort_flag = 1; atomicAdd(&b2k_tu_timeouts, 1u); }
-            break;
-          }
-        }
-        if (lane == 0) {
-          const int64_t n = (N - c * CE) < CE ? (N - c * CE) : CE;
-          const uint32_t bytes = (uint32_t)(n * (int64_t)sizeof(T));
-          mbar_arrive_expect_tx(&full[s], bytes);
-          bulk_g2s(dsm + (size_t)s * kCeChunkBytes, xr + c * CE, bytes, &full[s]);
-        }
-        ++issued;
-        if (++p_stage == S) { p_stage = 0; p_phase ^= 1u; }
-      }
-      __syncwarp();
-      if (!ok) break;
-    }
-  } else {
-    // ---- consumers
-    const int ct = threadIdx.x - 32;
-    const int cw = warp - 1;
-    int64_t u = 0;
-    int c_stage = 0;
-    uint32_t c_phase = 0;
-    int64_t t_next = nrows > 0 ? a.tgt[cid] : 0;
-    uint32_t nm = 0;  // rows merged so far (ignored rows are not merged)
-    // CTA 0, thread ct 0: merges the pending row (bounded wait for the other
-    // CTAs' pairs), writes its loss and frees its slot in every other CTA.
-    // The pending row's state lives in shared memory (one thread uses it).
-    auto merge_pending = [&]() -> bool {
-      const uint32_t pend_nm = pend_nm_s;
-      const int64_t pend_row = pend_row_s;
-      const float4 pend_v = pend_v_s;
-      const uint32_t par = pend_nm & 1u, ph = (pend_nm >> 1) & 1u;
-      bool ok = true;
-      if (P > 1) {
-        ok = mbar_wait_cluster(&merge_full[par], ph);
-        if (!ok) { abort_flag = 1; atomicAdd(&b2k_tu_timeouts, 1u); }
-      }
-      float m = pend_v.x, s = pend_v.y, xt = pend_v.z;
-      bool has = pend_v.w != 0.0f;
-      for (uint32_t r = 1; r < P; ++r) {
-        const volatile float* v = reinterpret_cast<volatile float*>(&slot[par][r]);
-        lse_merge(m, s, v[0], v[1]);
-        if (v[3] != 0.0f) { xt = v[2]; has = true; }
-      }
-      const float lse = m + (P32 ? logf(s) : f_log<false>(s));
-      static_cast<OutT*>(a.loss)[pend_row] =
-          from_f<OutT>(ok && has ? lse - xt : __int_as_float(0x7fc00000));
-      for (uint32_t r = 1; r < P; ++r) mbar_arrive_cluster(mapa_shared(&slot_free[par], r));
-      return ok;
-    };
-    for (int64_t i = 0; i < nrows; ++i) {
-      const int64_t row = cid + i * ncl;
-      const int64_t t = t_next;
-      if (i + 1 < nrows) t_next = a.tgt[row + ncl];
-      const bool ignore = (t == a.ignore);
-      if (ignore || t < 0 || t >= N) {
-        if (rank == 0 && ct == 0)
-          static_cast<OutT*>(a.loss)[row] =
-              from_f<OutT>(ignore ? 0.0f : __int_as_float(0x7fc00000));
-        continue;
-      }
-      const int64_t t_chunk = t / CE;
-      const int t_in = (int)(t - t_chunk * CE);
-      const bool has_t = t_chunk >= c0 && t_chunk < c1;
-      float m = -INFINITY, s = 0.0f;
-      for (int64_t c = c0; c < c1; ++c, ++u) {
-        const int st = c_stage;
-        bool ok = false;
-        if (!abort_flag) {
-          ok = mbar_wait(&full[st], c_phase);
-          if (!ok) { abort_flag = 1; atomicAdd(&b2k_tu_timeouts, 1u); }
-        }
-        if (ok) {
-          const T* cs = reinterpret_cast<const T*>(dsm + (size_t)st * kCeChunkBytes);
-          const int64_t left = N - c * CE;
-          const int n = (int)(left < CE ? left : CE);
-          if (ct == 0 && c == t_chunk) xt_s = to_f<T>(cs[t_in]);
-          float2 v[VPT][H];
-          if (n == CE) {
-#pragma unroll
-            for (int k = 0; k < VPT; ++k)
-              unpack2<T>(*reinterpret_cast<const uint4*>(cs + (k * NC + ct) * E), v[k]);
-          } else {
-#pragma unroll
-            for (int k = 0; k < VPT; ++k) {
-              const int idx = (k * NC + ct) * E;
-              if (idx < n) {
-                unpack2<T>(*reinterpret_cast<const uint4*>(cs + idx), v[k]);
-              } else {
-#pragma unroll
-                for (int j = 0; j < H; ++j) v[k][j] = f2s(-INFINITY);
-              }
-            }
-          }
-          auto sum_exp = [&](const float2 nz) {
-            float2 acc[VPT];
-#pragma unroll
-            for (int k = 0; k < VPT; ++k) {
-              acc[k] = f2s(0.0f);
-#pragma unroll
-              for (int j = 0; j < H; ++j) {
-                const float2 z = fma2(v[k][j], f2s(kLog2e), nz);
-                acc[k] = add2(acc[k], f2(ex2_approx(z.x), ex2_approx(z.y)));
-              }
-            }
-#pragma unroll
-            for (int k = 1; k < VPT; ++k) acc[0] = add2(acc[0], acc[k]);
-            return acc[0].x + acc[0].y;
-          };
-          bool done = false;
-          if constexpr (!P32) {
-            // lazy rescale, as in ce_tma_kernel
-            if (m != -INFINITY) {
-              const float part = sum_exp(f2s(-m * kLog2e));
-              if (part < 0x1p64f) { s += part; done = true; }
-            }
-          }
-          if (!done) {
-            float bmk[VPT];
-#pragma unroll
-            for (int k = 0; k < VPT; ++k) {
-              float t0 = fmaxf(v[k][0].x, v[k][0].y);
-#pragma unroll
-              for (int j = 1; j < H; ++j) t0 = fmaxf(t0, fmaxf(v[k][j].x, v[k][j].y));
-              bmk[k] = t0;
-            }
-            float bm = bmk[0];
-#pragma unroll
-            for (int k = 1; k < VPT; ++k) bm = fmaxf(bm, bmk[k]);
-            const float nmx = fmaxf(m, bm);
-            if (nmx != -INFINITY) {
-              if constexpr (P32) {
-                float acc = s * expf(m - nmx);
-#pragma unroll
-                for (int k = 0; k < VPT; ++k)
-#pragma unroll
-                  for (int j = 0; j < H; ++j)
-                    acc += expf(v[k][j].x - nmx) + expf(v[k][j].y - nmx);
-                s = acc;
-              } else {
-                s = fmaf(s, ex2_approx((m - nmx) * kLog2e), sum_exp(f2s(-nmx * kLog2e)));
-              }
-              m = nmx;
-            }
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
-        if (++c_stage == S) { c_stage = 0; c_phase ^= 1u; }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-        const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-        lse_merge(m, s, m2, s2);
-      }
-      if (lane == 0) { red_m[cw] = m; red_s[cw] = s; }
-      named_bar_sync(1, NC);
-      if (ct == 0) {
-        float Mx = red_m[0], Ssum = red_s[0];
-        for (int w = 1; w < kCeConsumerWarps; ++w) lse_merge(Mx, Ssum, red_m[w], red_s[w]);
-        const float xt = has_t ? xt_s : 0.0f;
-        if (!abort_flag) {
-          if (rank == 0) {
-            if (pend_s) merge_pending();
-            pend_s = 1;
-            pend_row_s = row;
-            pend_nm_s = nm;
-            pend_v_s = make_float4(Mx, Ssum, xt, has_t ? 1.0f : 0.0f);
-          } else {
-            const uint32_t par = nm & 1u;
-            bool ok = true;
-            if (nm >= 2) {
-              ok = mbar_wait_cluster(&slot_free[par], ((nm - 2) >> 1) & 1u);
-              if (!ok) { abort_flag = 1; atomicAdd(&b2k_tu_timeouts, 1u); }
-            }
-            if (ok) {
-              st_cluster_f32x4(mapa_shared(&slot[par][rank], 0), Mx, Ssum, xt,
-                               has_t ? 1.0f : 0.0f);
-              mbar_arrive_cluster(mapa_shared(&merge_full[par], 0));
-            }
-          }
-        }
-        ++nm;
-        stop = abort_flag;
-      }
-      named_bar_sync(1, NC);
-      if (stop) break;
-    }
-    if (ct == 0) {
-      if (rank == 0 && pend_s && !abort_flag) merge_pending();
-      consumed = u;
-    }
-  }
-  __syncthreads();
-  // after an abort, wait (bounded) for copies still in flight
-  if (threadIdx.x == 0)
-    for (int64_t j = consumed; j < issued; ++j)
-      mbar_wait(&full[(int)(j % S)], (uint32_t)((j / S) & 1));
-  // no CTA leaves while another may still write its shared memory
-  cluster_sync_all();
-}
-
 // Rows of 4..64 KB (the spec shapes, V up to 32768 at 2 bytes): whole rows
 // through the persistent bulk-copy row pipeline; each thread takes a local
 // (max, sum-exp) over its slice, one block reduction per row, the target
@@ -839,60 +546,6 @@ static int ce_env(const char* name, int dflt) {
   return s ? atoi(s) : dflt;
 }
 
-// Launches ce_split_kernel with clusters of P CTAs, as many clusters as can be
-// resident at once (each walks its rows, so a cluster that had to wait for a
-// slot would add a round to the tail).  False when the cluster shape cannot
-// be launched (the caller uses ce_tma_kernel).
-template <typename T, typename OutT>
-static bool ce_launch_split(const CeArgs& a, cudaStream_t st, int S, int P, size_t smem) {
-  auto kern = ce_split_kernel<T, OutT>;
-  cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(kCeThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)P;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  // resident clusters, cached per (device, P, S)
-  static std::mutex mu;
-  static int cache_key[64], cache_val[64], ncache = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int key = (dev << 16) | (P << 8) | S;
-  int ncl = -1;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    for (int i = 0; i < ncache; ++i)
-      if (cache_key[i] == key) ncl = cache_val[i];
-  }
-  if (ncl < 0) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cfg.gridDim = dim3((unsigned)P, 1, 1);
-    if (cudaOccupancyMaxActiveClusters(&ncl, kern, &cfg) != cudaSuccess) {
-      cudaGetLastError();
-      ncl = 0;
-    }
-    std::lock_guard<std::mutex> lock(mu);
-    if (ncache < 64) {
-      cache_key[ncache] = key;
-      cache_val[ncache++] = ncl;
-    }
-  }
-  if (ncl < 1) return false;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (ncl > a.M) ncl = (int)a.M;
-  cfg.gridDim = dim3((unsigned)(ncl * P), 1, 1);
-  if (cudaLaunchKernelEx(&cfg, kern, a, S) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  return true;
-}
-
 // Launches the row-loss kernel; with a.dx set, the pipelined kernel also
 // writes the gradient (*bwd_done = true), the rows kernel does not.
 template <typename T, typename OutT>
@@ -924,22 +577,6 @@ static int ce_launch(const CeArgs& a, cudaStream_t st, bool* bwd_done = nullptr)
     const int S = a.dx ? S_bwd : S_fwd;
     const int cps = a.dx ? cps_bwd : cps_fwd;
     const size_t smem = (size_t)S * kCeChunkBytes + 2 * (size_t)S * sizeof(uint64_t);
-    if (!a.dx) {
-      // few rows per block: share each row between the CTAs of a cluster
-      // (B2K_CE_SPLIT: 2..8 CTAs per row, -1 = by rows per block, 0 = off,
-      // the default: at 4096 x 128256 bf16 the split kernel measured 0.267
-      // ms with 4 CTAs per row and 0.202 ms with 2 against 0.176 ms for
-      // whole rows, CTA 0's per-row merge holding up its consumers)
-      static const int split_knob = ce_env("B2K_CE_SPLIT", 0);
-      const int64_t nchunks = (a.N * (int64_t)sizeof(T) + kCeChunkBytes - 1) / kCeChunkBytes;
-      const double per_block = (double)a.M / ((double)sm_count() * cps);
-      int P = 0;
-      if (split_knob >= 2 && split_knob <= kCeMaxSplit) P = split_knob;
-      else if (split_knob < 0) P = per_block < 12.0 ? 4 : (per_block < 24.0 ? 2 : 0);
-      while (P > nchunks) P >>= 1;
-      if (P >= 2 && ce_launch_split<T, OutT>(a, st, S, P, smem))
-        return check_launch("b2k_cross_entropy(split)");
-    }
     // balanced grid: the fewest blocks that still give each block
     // ceil(M / resident blocks) rows, so every block walks the same number
     // of rows (4096 rows on 444 resident blocks: 410 blocks of 10 rows

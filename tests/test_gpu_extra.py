@@ -282,13 +282,12 @@ def test_two_devices_in_one_process():
 
 @pytest.mark.parametrize("dt", DTS)
 @pytest.mark.parametrize("M", [3, 700, 2000, 8000])
-def test_cross_entropy_rows_shared_by_a_cluster(dt, M):
-    """Long rows with few rows per resident block (a vocabulary-sized shard
-    on one of many GPUs): each row is split over the CTAs of a cluster, 4 per
-    row below 12 rows per block, 2 below 24, and the (max, sum-exp) pairs
-    meet in distributed shared memory.  Sampled rows against the oracle,
-    including ignored rows, a bad target (NaN) and targets in the first and
-    last chunk of a row, plus the mean over all rows."""
+def test_cross_entropy_few_rows_per_block(dt, M):
+    """Vocabulary-length rows with few rows per resident block (a shard of
+    the logits on one of many GPUs; the grid is balanced so every block walks
+    the same number of rows).  Sampled rows against the oracle, including
+    ignored rows, a bad target (NaN) and targets in the first and last chunk
+    of a row, plus the mean over all rows."""
     V = 128256
     g = torch.Generator(device="cuda").manual_seed(M)
     x = (torch.randn((M, V), generator=g, device="cuda") * 3).to(TDT[dt])
@@ -317,3 +316,28 @@ def test_cross_entropy_rows_shared_by_a_cluster(dt, M):
                                                      ignore_index=-100, reduction="sum"))
         c += int((t[r:r + 1024] != -100).sum())
     assert abs(got - s / c) <= 1e-3 * abs(s / c), (got, s / c)
+
+
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("op", ["entropy", "kl_div", "cumsum"])
+@pytest.mark.parametrize("shape,scale", [((3000, 1024), 1.0), ((700, 8192), 8.0),
+                                         ((333, 4096), 64.0), ((64, 512), 1.0)])
+def test_reductions_pipelined(dt, op, shape, scale):
+    """entropy / kl_div / cumsum on aligned rows whose inputs fit one ring
+    stage (the bulk-copy pipelined kernels: one merge of (max, sum, weighted
+    sum) per row, fp32 run + fp64 thread offsets for the scan), at scales
+    1 / 8 / 64 and more rows than resident blocks, against the oracle on
+    sampled rows (all rows for the small case)."""
+    M, N = shape
+    if dt == "f32" and N * 4 * (2 if op == "kl_div" else 1) > (64 << 10):
+        pytest.skip("row above one ring stage: the register / streaming kernels")
+    kind = regimes.OPS[op].kind
+    case = regimes.make_case(kind, 17, M, N, dt, scale)
+    ins = to_cuda(case)
+    out = b200k.get_op(op)(*ins)
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([[0, M - 1], np.arange(0, M, max(1, M // 23))]))
+    sub = [(v[rows] if v.ndim == 2 else v, tag) for v, tag in case]
+    ref = regimes.reference(op, sub)
+    ok, err, bad = allclose_report(out.float().cpu().numpy()[rows], ref, *tol_for(op, dt))
+    assert ok, f"{op} {dt} {shape} x{scale}: max err {err}, {bad} bad"
