@@ -363,7 +363,6 @@ struct RedSlice {
     t = 0.0f;
     if (m == -INFINITY) return;
     float2 s2 = f2s(0.0f), t2 = f2s(0.0f);
-    const float2 nz = f2s(-m * kLog2e);
 #pragma unroll
     for (int v = 0; v < V; ++v)
       if (in[v])
@@ -373,7 +372,12 @@ struct RedSlice {
           if constexpr (P) {
             e = f2(expf(x[v][j].x - m), expf(x[v][j].y - m));
           } else {
-            const float2 z = fma2(x[v][j], f2s(kLog2e), nz);
+            // x - m first (exact for the terms near the max), then the scale
+            // to base 2: fma(x, log2e, -m log2e) would carry an absolute
+            // error of |x| 2^-24 into every exponent, and the x-weighted sums
+            // here (x up to +-256 at the spec's stress scale) turn that into
+            // 1e-3-level errors of entropy / kl
+            const float2 z = mul2(sub2(x[v][j], f2s(m)), f2s(kLog2e));
             e = f2(ex2_approx(z.x), ex2_approx(z.y));
           }
           s2 = add2(s2, e);
