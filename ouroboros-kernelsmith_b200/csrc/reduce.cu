@@ -282,43 +282,48 @@ __global__ void __launch_bounds__(kRedMaxThreads) cumsum_kernel(const RowRedArgs
 //    fp32, and the block scans the per-thread totals in fp64; an output is
 //    the thread's fp64 offset (rounded once to fp32) plus its local prefix.
 
-// merge of K floats across the block (one row per block), every thread gets
-// the result; red holds K * 32 floats
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// merge of K floats across the warps of the block when every lane of a warp
+// already holds its warp's value (one row per block); every thread gets the
+// result; red holds K * 32 floats
 template <int K, typename Merge>
-__device__ __forceinline__ void block_merge(float (&v)[K], const float (&ident)[K], float* red,
+__device__ __forceinline__ void xwarp_merge(float (&v)[K], const float (&ident)[K], float* red,
                                             Merge merge) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (nw == 1) return;
+  if (lane == 0)
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    float u[K];
+    for (int k = 0; k < K; ++k) red[k * 32 + w] = v[k];
+  __syncthreads();
+  if (w == 0) {
 #pragma unroll
-    for (int k = 0; k < K; ++k) u[k] = __shfl_xor_sync(0xffffffffu, v[k], o);
-    merge(v, u);
-  }
-  if (nw > 1) {
+    for (int k = 0; k < K; ++k) v[k] = lane < nw ? red[k * 32 + lane] : ident[k];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      if (o >= nw) continue;
+      float u[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) u[k] = __shfl_xor_sync(0xffffffffu, v[k], o);
+      merge(v, u);
+    }
     if (lane == 0)
 #pragma unroll
-      for (int k = 0; k < K; ++k) red[k * 32 + w] = v[k];
-    __syncthreads();
-    if (w == 0) {
-#pragma unroll
-      for (int k = 0; k < K; ++k) v[k] = lane < nw ? red[k * 32 + lane] : ident[k];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        float u[K];
-#pragma unroll
-        for (int k = 0; k < K; ++k) u[k] = __shfl_xor_sync(0xffffffffu, v[k], o);
-        merge(v, u);
-      }
-      if (lane == 0)
-#pragma unroll
-        for (int k = 0; k < K; ++k) red[k * 32] = v[k];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < K; ++k) v[k] = red[k * 32];
-    __syncthreads();  // red is reused by the next row
+      for (int k = 0; k < K; ++k) red[k * 32] = v[k];
   }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < K; ++k) v[k] = red[k * 32];
+  __syncthreads();  // red is reused by the next row
 }
 
 template <bool P>
@@ -427,10 +432,14 @@ __global__ void __launch_bounds__(kRedMaxThreads) entropy_tma_kernel(const RowRe
 #pragma unroll
         for (int j = 0; j < H; ++j) xv[v][j] = f2s(0.0f);
     }
+    // the warp's max first (no exponentials in the shuffle stages), the sums
+    // against it, warp sums, then one merge of the warps' triples
     float r[3];
-    r[0] = Sl::vmax(xv, in);
+    r[0] = warp_max(Sl::vmax(xv, in));
     Sl::sums(xv, nullptr, in, r[0], r[1], r[2]);
-    block_merge<3>(r, ident, red, [](float (&p)[3], const float (&q)[3]) {
+    r[1] = warp_sum(r[1]);
+    r[2] = warp_sum(r[2]);
+    xwarp_merge<3>(r, ident, red, [](float (&p)[3], const float (&q)[3]) {
       lse_merge_k<P, 3>(p, q);
     });  // barriers inside: every thread has read the stage
     if (abort_flag) break;
@@ -493,12 +502,15 @@ __global__ void __launch_bounds__(kRedMaxThreads) kl_tma_kernel(const RowRedArgs
       }
     }
     float r[5];
-    r[0] = Sl::vmax(xv, in);
+    r[0] = warp_max(Sl::vmax(xv, in));
     Sl::sums(xv, yv, in, r[0], r[1], r[2]);
-    r[3] = Sl::vmax(yv, in);
+    r[3] = warp_max(Sl::vmax(yv, in));
     float unused;
     Sl::sums(yv, nullptr, in, r[3], r[4], unused);
-    block_merge<5>(r, ident, red, merge5);
+    r[1] = warp_sum(r[1]);
+    r[2] = warp_sum(r[2]);
+    r[4] = warp_sum(r[4]);
+    xwarp_merge<5>(r, ident, red, merge5);
     if (abort_flag) break;
     pipe.refill();
     if (tx == 0) {
@@ -597,7 +609,9 @@ __global__ void __launch_bounds__(kRedMaxThreads) cumsum_tma_kernel(const RowRed
 
 // The pipelined kernels, when the rows are aligned and a ring stage (all
 // inputs of one row) is at most 64 KB: kind 0 entropy, 1 kl_div, 2 cumsum.
-// Threads per row: two 16-byte vectors each while that fits 512 threads.
+// Threads per row: B2K_RED_VPT 16-byte vectors each (2 or 4; default 4 for
+// entropy and cumsum, 2 for kl_div, whose two inputs double the registers)
+// while that fits 64..512 threads.
 template <typename T>
 static bool rowred_try_tma(const RowRedArgs& a, int kind, cudaStream_t st) {
   constexpr int E = Traits<T>::E;
@@ -605,12 +619,18 @@ static bool rowred_try_tma(const RowRedArgs& a, int kind, cudaStream_t st) {
     const char* s = getenv("B2K_TMA");
     return s ? atoi(s) : 1;
   }();
+  static const int vpt_knob = [] {
+    const char* s = getenv("B2K_RED_VPT");
+    const int v = s ? atoi(s) : 0;
+    return v == 2 || v == 4 ? v : 0;
+  }();
   if (!use_tma || !a.aligned) return false;
   const int64_t nvec = a.N / E;
   const int nin = kind == 1 ? 2 : 1;
   const int64_t row_bytes = (int64_t)a.N * (int64_t)sizeof(T);
   if (nvec < 64 || nin * row_bytes > (64 << 10)) return false;
-  int G = next_pow2((nvec + 1) / 2);
+  const int vpt = vpt_knob ? vpt_knob : (kind == 1 ? 2 : 4);
+  int G = next_pow2((nvec + vpt - 1) / vpt);
   G = G < 64 ? 64 : (G > kRedMaxThreads ? kRedMaxThreads : G);
   const int64_t vneed = (nvec + G - 1) / G;
   if (vneed > 4) return false;
