@@ -635,9 +635,14 @@ static bool rowred_try_tma(const RowRedArgs& a, int kind, cudaStream_t st) {
   const int64_t vneed = (nvec + G - 1) / G;
   if (vneed > 4) return false;
   const bool v2 = vneed <= 2;
+  static const int want_stages = [] {
+    const char* s = getenv("B2K_TMA_STAGES");
+    const int v = s ? atoi(s) : 0;
+    return v >= 2 && v <= 8 ? v : 2;
+  }();
   auto go = [&](auto kern, int n_in) -> bool {
     PipeShape ps;
-    if (!choose_pipe_shape(kern, G, n_in * row_bytes, 0, 2, &ps)) return false;
+    if (!choose_pipe_shape(kern, G, n_in * row_bytes, 0, want_stages, &ps)) return false;
     const size_t smem = (size_t)ps.S * n_in * (size_t)row_bytes + (size_t)ps.S * sizeof(uint64_t);
     int64_t grid = (int64_t)sm_count() * ps.cps;
     if (grid > a.M) grid = a.M;
