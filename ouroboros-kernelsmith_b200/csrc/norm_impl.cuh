@@ -373,19 +373,14 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
   RowPipe<NIN> pipe;
   pipe.init(dsm, S, a.M, (uint32_t)N * (uint32_t)sizeof(T), srcs, lds, (int)sizeof(T));
 
-  // weight and bias staged once per block in shared memory behind the ring
-  // and read per row: held in registers across the row loop they took 32 of
-  // the 128 registers of the 4-vector LayerNorm (64 with them here), which
-  // limited it to 4 blocks of 128 threads per SM
-  T* wsm = reinterpret_cast<T*>(dsm + RowPipe<NIN>::tail_offset(S, (int64_t)N * sizeof(T)));
-  T* bsm = wsm + (HAS_W ? N : 0);
-  for (int c = g.tx * E; c < N; c += g.G * E) {
-    if constexpr (HAS_W)
-      *reinterpret_cast<uint4*>(wsm + c) = ld_keep(static_cast<const T*>(a.w) + c);
-    if constexpr (MODE == NM_LN)
-      *reinterpret_cast<uint4*>(bsm + c) = ld_keep(static_cast<const T*>(a.b) + c);
+  // weight slices stay in registers (raw 16-byte vectors) for every row
+  uint4 wraw[V], braw[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * g.G + g.tx) * E;
+    wraw[v] = (HAS_W && c < N) ? ld_keep(static_cast<const T*>(a.w) + c) : zero4();
+    braw[v] = (MODE == NM_LN && c < N) ? ld_keep(static_cast<const T*>(a.b) + c) : zero4();
   }
-  __syncthreads();
 
   int64_t k = 0;
   for (; k < pipe.nrows; ++k) {
@@ -435,8 +430,8 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
       const int c = (v * g.G + g.tx) * E;
       if (c < N) {
         float2 wv[H], bv[H], out[H];
-        if constexpr (HAS_W) unpack2<T>(*reinterpret_cast<const uint4*>(wsm + c), wv);
-        if constexpr (MODE == NM_LN) unpack2<T>(*reinterpret_cast<const uint4*>(bsm + c), bv);
+        if constexpr (HAS_W) unpack2<T>(wraw[v], wv);
+        if constexpr (MODE == NM_LN) unpack2<T>(braw[v], bv);
 #pragma unroll
         for (int j = 0; j < H; ++j)
           out[j] = norm_pair<T, MODE, ACT>(hv[v][j], nmu2, rs2, HAS_W ? wv[j] : f2s(1.0f),
@@ -641,15 +636,10 @@ static bool norm_try_tma(const NormArgs& a, cudaStream_t st, int* status) {
   // stages): more blocks in flight beat a deeper ring per block
   int want_stages = a.tma_stages;
   if (want_stages <= 0) want_stages = 2;
-  // weight and bias kept in shared memory behind the ring
-  const int64_t wb_bytes =
-      ((MODE != NM_L2 ? 1 : 0) + (MODE == NM_LN ? 1 : 0)) * a.N * (int64_t)sizeof(T);
   PipeShape ps;
-  if (!choose_pipe_shape(kern, G, stage, a.tma_cps, want_stages, &ps, wb_bytes + 16))
-    return false;
+  if (!choose_pipe_shape(kern, G, stage, a.tma_cps, want_stages, &ps)) return false;
   const int cps = ps.cps, S = ps.S;
-  const size_t smem =
-      RowPipe<RESID ? 2 : 1>::tail_offset(S, a.N * (int64_t)sizeof(T)) + (size_t)wb_bytes;
+  const size_t smem = RowPipe<RESID ? 2 : 1>::smem_bytes(S, a.N * (int64_t)sizeof(T));
   int64_t grid = (int64_t)sms * cps;
   if (grid > a.M) grid = a.M;
   launch_pdl(kern, (unsigned)grid, (unsigned)G, smem, st, a, S);

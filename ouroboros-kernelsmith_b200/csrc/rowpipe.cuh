@@ -37,12 +37,6 @@ struct RowPipe {
   static size_t smem_bytes(int S, int64_t row_bytes) {
     return (size_t)S * NIN * (size_t)row_bytes + (size_t)S * sizeof(uint64_t);
   }
-  // 16-byte aligned offset just past the ring and its barriers (where a
-  // kernel may keep its own per-block data)
-  __host__ __device__ static size_t tail_offset(int S, int64_t row_bytes) {
-    return ((size_t)S * NIN * (size_t)row_bytes + (size_t)S * sizeof(uint64_t) + 15) &
-           ~(size_t)15;
-  }
 
   __device__ __forceinline__ void issue(int64_t k) {
     const int s = istage;
@@ -184,16 +178,14 @@ inline void allow_max_dynamic_smem(Kernel kern) {
 
 template <typename Kernel>
 inline bool choose_pipe_shape_uncached(Kernel kern, int threads, int64_t stage_bytes,
-                                       int want_cps, int want_stages, PipeShape* ps,
-                                       int64_t extra) {
+                                       int want_cps, int want_stages, PipeShape* ps) {
   const int64_t budget = 200 << 10;  // dynamic shared memory per SM
-  auto need = [&](int cps, int S) { return (int64_t)cps * (S * stage_bytes + extra); };
   if (want_cps > 0) {
     int cps = want_cps;
     int S = want_stages > 0 ? want_stages : 4;
-    while (S > 2 && need(cps, S) > budget) --S;
-    while (cps > 1 && need(cps, S) > budget) --cps;
-    if (need(cps, S) > budget) return false;
+    while (S > 2 && (int64_t)cps * S * stage_bytes > budget) --S;
+    while (cps > 1 && (int64_t)cps * S * stage_bytes > budget) --cps;
+    if ((int64_t)cps * S * stage_bytes > budget) return false;
     ps->cps = cps;
     ps->S = S;
     return true;
@@ -201,10 +193,9 @@ inline bool choose_pipe_shape_uncached(Kernel kern, int threads, int64_t stage_b
   // blocks per SM: as many as are resident, each with want_stages (else 4)
   for (int cps = 8; cps >= 1; --cps) {
     int S = want_stages > 0 ? want_stages : 4;
-    while (S > 2 && need(cps, S) > budget) --S;
-    if (need(cps, S) > budget) continue;
-    const size_t smem =
-        (size_t)S * (size_t)stage_bytes + (size_t)S * sizeof(uint64_t) + 16 + (size_t)extra;
+    while (S > 2 && (int64_t)cps * S * stage_bytes > budget) --S;
+    if ((int64_t)cps * S * stage_bytes > budget) continue;
+    const size_t smem = (size_t)S * (size_t)stage_bytes + (size_t)S * sizeof(uint64_t);
     int resident = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, threads, smem) !=
         cudaSuccess) {
@@ -220,16 +211,15 @@ inline bool choose_pipe_shape_uncached(Kernel kern, int threads, int64_t stage_b
   return false;
 }
 
-// Cached per (device, kernel, threads, stage bytes, overrides, extra bytes):
-// the occupancy query runs once, later launches pay a table lookup.  `extra`
-// is per-block shared memory the kernel keeps behind the ring.
+// Cached per (device, kernel, threads, stage bytes, overrides): the occupancy
+// query runs once, later launches pay a table lookup.
 template <typename Kernel>
 inline bool choose_pipe_shape(Kernel kern, int threads, int64_t stage_bytes, int want_cps,
-                              int want_stages, PipeShape* ps, int64_t extra = 0) {
+                              int want_stages, PipeShape* ps) {
   struct Entry {
     const void* k;
     int dev, threads, cps, stages;
-    int64_t stage, extra;
+    int64_t stage;
     PipeShape ps;
     bool ok;
   };
@@ -244,20 +234,17 @@ inline bool choose_pipe_shape(Kernel kern, int threads, int64_t stage_bytes, int
     for (int i = 0; i < n; ++i) {
       const Entry& e = cache[i];
       if (e.k == (const void*)kern && e.dev == dev && e.threads == threads &&
-          e.stage == stage_bytes && e.cps == want_cps && e.stages == want_stages &&
-          e.extra == extra) {
+          e.stage == stage_bytes && e.cps == want_cps && e.stages == want_stages) {
         *ps = e.ps;
         return e.ok;
       }
     }
   }
   PipeShape r{1, 2};
-  const bool ok =
-      choose_pipe_shape_uncached(kern, threads, stage_bytes, want_cps, want_stages, &r, extra);
+  const bool ok = choose_pipe_shape_uncached(kern, threads, stage_bytes, want_cps, want_stages, &r);
   std::lock_guard<std::mutex> lock(mu);
   if (n < 512)
-    cache[n++] =
-        Entry{(const void*)kern, dev, threads, want_cps, want_stages, stage_bytes, extra, r, ok};
+    cache[n++] = Entry{(const void*)kern, dev, threads, want_cps, want_stages, stage_bytes, r, ok};
   *ps = r;
   return ok;
 }
