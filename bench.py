@@ -992,6 +992,10 @@ def run_grid(args, device):
                              if args.grid_compile else []):
                     key = "compile" if mode == "default" else mode
                     try:
+                        # a fresh dynamo cache per cell: the reference expression
+                        # is the same function for every cell, and past the
+                        # recompile limit dynamo would run it eagerly
+                        torch._dynamo.reset()
                         fn = torch.compile(e, mode=mode, dynamic=False)
                         for _ in range(3):
                             fn(*probe)
@@ -1174,6 +1178,7 @@ def measure_compile(wl, stream, mode, steps=10):
     the compiled code cannot be captured), or a one-line reason when that
     baseline cannot be had."""
     try:
+        torch._dynamo.reset()  # a fresh cache: no recompile limit carried over
         st = wl.compile_step(mode)
         if st is None:
             return None, "not compiled: the step runs autograd"

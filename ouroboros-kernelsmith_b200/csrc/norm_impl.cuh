@@ -143,6 +143,66 @@ __device__ __forceinline__ void group_moments(float& n, float& m, float& q, cons
   }
 }
 
+// LayerNorm statistics of a staged row from sums shifted by K, the row's
+// first value (the same in every thread): S = sum (h - K), Q = sum (h - K)^2,
+// mean = K + S/N, var = Q/N - (S/N)^2.  Two plain sums in one block reduction:
+// no division per merge step and about half the dependent instructions of
+// the Chan merge, which bounds these kernels on rows of a few KB.  K is an
+// element of the row, so |K - mean| is at most the row's largest deviation
+// and the cancellation in Q/N - (S/N)^2 costs at most log2((largest
+// deviation / std)^2) bits (a single 1e4 outlier in a unit row of 4096: a
+// relative error of ~2e-4 in the variance).  Slots are whole (aligned rows).
+template <int V, int H>
+__device__ __forceinline__ void ln_stats_shift(const float2 (&hv)[V][H], int N, const Group& g,
+                                               float* red, float eps, float K, float& mu,
+                                               float& rs) {
+  constexpr int E = 2 * H;
+  float2 s2 = f2s(0.0f), q2 = f2s(0.0f);
+  const float2 nk = f2s(-K);
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * g.G + g.tx) * E;
+    if (c < N) {
+#pragma unroll
+      for (int j = 0; j < H; ++j) {
+        const float2 d = add2(hv[v][j], nk);
+        s2 = add2(s2, d);
+        q2 = fma2(d, d, q2);
+      }
+    }
+  }
+  float s = s2.x + s2.y, q = q2.x + q2.y;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    q += __shfl_xor_sync(0xffffffffu, q, o);
+  }
+  if (g.G > 32) {
+    const int nw = g.G >> 5, w = g.tx >> 5, lane = g.tx & 31;
+    if (lane == 0) { red[w] = s; red[512 + w] = q; }
+    __syncthreads();
+    if (w == 0) {
+      float a = lane < nw ? red[lane] : 0.0f;
+      float b = lane < nw ? red[512 + lane] : 0.0f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+        if (o < nw) {
+          a += __shfl_xor_sync(0xffffffffu, a, o);
+          b += __shfl_xor_sync(0xffffffffu, b, o);
+        }
+      if (lane == 0) { red[0] = a; red[512] = b; }
+    }
+    __syncthreads();
+    s = red[0];
+    q = red[512];
+    __syncthreads();
+  }
+  const float inv = 1.0f / (float)N;
+  const float ms = s * inv;
+  mu = K + ms;
+  rs = rsqrtf(fmaxf(fmaf(q, inv, -ms * ms), 0.0f) + eps);
+}
+
 // Statistics of a row slice held as pairs hv[V][H] (slot v covers elements
 // [(v*G+tx)*E, +E)); out-of-range elements hold 0.  `whole` = every slot is
 // either entirely inside or entirely outside the row (aligned rows).
@@ -418,7 +478,14 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
       }
     }
     float mu, rs;
-    row_stats<MODE, V, H>(hv, N, true, g, red, a.eps, mu, rs);
+    if constexpr (MODE == NM_LN) {
+      // the row's first value (x + r as the threads formed it), from the stage
+      float K = to_f<T>(xs[0]);
+      if constexpr (RESID) K += to_f<T>(rsm[0]);
+      ln_stats_shift<V, H>(hv, N, g, red, a.eps, K, mu, rs);
+    } else {
+      row_stats<MODE, V, H>(hv, N, true, g, red, a.eps, mu, rs);
+    }
     // the reduction's barriers order every thread's reads of the stage
     // before the refill
     if (abort_flag) break;
