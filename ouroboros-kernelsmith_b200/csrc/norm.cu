@@ -15,9 +15,10 @@ static int env_int(const char* name, int dflt) {
 // register path, power of two <= 512), B2K_TMA (0 disables the bulk-copy
 // path), B2K_TMA_THREADS, B2K_TMA_CPS (blocks per SM), B2K_TMA_STAGES,
 // B2K_L2PF_ROWS (rows per block of the bulk-copy path hinted into L2 before
-// the kernel waits for its predecessor; 0 = off).
+// the kernel waits for its predecessor; 0 = off), B2K_LN_SHIFT (LayerNorm
+// statistics of the bulk-copy path: 1 shifted sums, 0 Chan's merge).
 struct NormKnobs {
-  int g_target, use_tma, tma_threads, tma_cps, tma_stages, l2pf;
+  int g_target, use_tma, tma_threads, tma_cps, tma_stages, l2pf, ln_shift;
   NormKnobs() {
     const int t = env_int("B2K_NORM_TPR", 0);
     g_target = (t >= 1 && t <= kNormMaxThreads && (t & (t - 1)) == 0) ? t : 128;
@@ -29,6 +30,7 @@ struct NormKnobs {
     const int st = env_int("B2K_TMA_STAGES", 0);
     tma_stages = (st >= 2 && st <= 8) ? st : 0;
     l2pf = l2_prefetch_rows_knob();
+    ln_shift = env_int("B2K_LN_SHIFT", 1) != 0;
   }
 };
 
@@ -108,6 +110,7 @@ extern "C" int b2k_norm(const void* x, int64_t ldx, const void* r, int64_t ldr, 
   a.tma_cps = kn.tma_cps;
   a.tma_stages = kn.tma_stages;
   a.l2_prefetch_rows = kn.l2pf;
+  a.ln_shift = kn.ln_shift;
   const int es = dtype_size(dtype);
   const int E = es ? 16 / es : 1;
   bool al = (N % E == 0) && aligned16(x) && aligned16(y) && ((ldx * es) % 16 == 0) &&

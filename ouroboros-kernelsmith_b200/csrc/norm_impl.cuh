@@ -55,6 +55,7 @@ struct NormArgs {
   int tma_stages;  // pipeline depth (0 = automatic)
   int use_tma;     // 0 disables the bulk-copy path
   int l2_prefetch_rows;  // bulk-copy path: rows per block hinted into L2 before the wait
+  int ln_shift;          // bulk-copy path: LayerNorm statistics from shifted sums (else Chan)
 };
 
 constexpr int kNormMaxThreads = 512;
@@ -478,7 +479,7 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
       }
     }
     float mu, rs;
-    if constexpr (MODE == NM_LN) {
+    if (MODE == NM_LN && a.ln_shift) {
       // the row's first value (x + r as the threads formed it), from the stage
       float K = to_f<T>(xs[0]);
       if constexpr (RESID) K += to_f<T>(rsm[0]);
