@@ -16,7 +16,8 @@ static int env_int(const char* name, int dflt) {
 // path), B2K_TMA_THREADS, B2K_TMA_CPS (blocks per SM), B2K_TMA_STAGES,
 // B2K_L2PF_ROWS (rows per block of the bulk-copy path hinted into L2 before
 // the kernel waits for its predecessor; 0 = off), B2K_LN_SHIFT (LayerNorm
-// statistics of the bulk-copy path: 1 shifted sums, 0 Chan's merge).
+// statistics of the bulk-copy path: 0 Chan's merge, 2 shifted sums, 1 by
+// shape).
 struct NormKnobs {
   int g_target, use_tma, tma_threads, tma_cps, tma_stages, l2pf, ln_shift;
   NormKnobs() {
@@ -30,7 +31,8 @@ struct NormKnobs {
     const int st = env_int("B2K_TMA_STAGES", 0);
     tma_stages = (st >= 2 && st <= 8) ? st : 0;
     l2pf = l2_prefetch_rows_knob();
-    ln_shift = env_int("B2K_LN_SHIFT", 1) != 0;
+    const int sh = env_int("B2K_LN_SHIFT", 1);
+    ln_shift = sh >= 0 && sh <= 2 ? sh : 1;
   }
 };
 

@@ -471,10 +471,7 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
       }
     }
     // the shift of the LayerNorm sums: the row's first value (x + r as the
-    // threads formed it), read from the stage BEFORE the residual-stream
-    // stores below — behind them, this shared-memory load waits for the
-    // stores to leave the memory pipe (measured 0.99 -> 0.87 of the copy
-    // peak at 16384 x 8192 with h written)
+    // threads formed it), read from the stage
     float K = 0.0f;
     if (MODE == NM_LN && a.ln_shift) {
       K = to_f<T>(xs[0]);
@@ -717,7 +714,16 @@ static bool norm_try_tma(const NormArgs& a, cudaStream_t st, int* status) {
   const size_t smem = RowPipe<RESID ? 2 : 1>::smem_bytes(S, a.N * (int64_t)sizeof(T));
   int64_t grid = (int64_t)sms * cps;
   if (grid > a.M) grid = a.M;
-  launch_pdl(kern, (unsigned)grid, (unsigned)G, smem, st, a, S);
+  // LayerNorm statistics (B2K_LN_SHIFT: 0 Chan's merge, 2 shifted sums, 1 =
+  // by shape): shifted sums, except when the residual stream is written and
+  // each block walks 12 rows or more, where Chan's merge measured faster
+  // (16384 x 8192 bf16 with h: 0.988 against 0.868 of the copy peak; 2048
+  // rows: 0.864 against 0.915; without h the shifted sums win at every shape,
+  // LayerNorm 8192 x 4096 bf16 0.81 against 0.64)
+  NormArgs b = a;
+  if (MODE == NM_LN && a.ln_shift == 1)
+    b.ln_shift = (a.h == nullptr || a.M < 12 * grid) ? 1 : 0;
+  launch_pdl(kern, (unsigned)grid, (unsigned)G, smem, st, b, S);
   *status = check_launch("b2k_norm(tma)");
   return true;
 }
