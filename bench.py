@@ -442,12 +442,14 @@ class CrossEntropy(Workload):
     def setup(self, device, rank, world):
         super().setup(device, rank, world)
         self.exchange = "none (1 rank)"
-        if world > 1 and type(self) is CrossEntropy:
-            # collective set-up of the peer-memory exchange (every rank, same order):
-            # row losses + fused reduce / exchange / mean = 2 launches per step
+        if world > 1:
+            # collective set-up of the peer-memory exchange (every rank, same order)
             from b200k.dist import ce_exchange
             if ce_exchange(None, device) is not None:
-                self.launches_per_step = 2
+                # mean: row losses + fused reduce / exchange / mean; loss +
+                # gradient: valid count, count exchange, fused kernel, fused
+                # reduce / exchange / mean
+                self.launches_per_step = 2 if type(self) is CrossEntropy else 4
                 self.exchange = "peer memory (CUDA IPC over NVLink), fused into the reduce kernel"
             else:
                 self.exchange = "NCCL all-reduce"
@@ -556,11 +558,6 @@ class CrossEntropyFwdBwd(CrossEntropy):
     in one pass over the logits."""
     name = "cross_entropy_fwd_bwd"
     launches_per_step = 4  # valid count, fused fwd+bwd, shard reduce, mean
-
-    def setup(self, device, rank, world):
-        super().setup(device, rank, world)
-        # two NCCL all-reduces per step when sharded: launched step by step
-        self.graphable = world == 1
 
     def run(self, x, t):
         return self.b2k.cross_entropy_fwd_bwd(x, t)

@@ -211,8 +211,11 @@ int64_t b2k_ce_exchange_bytes(int world);
  * stores this rank's pair into every rank's buffer, publishes it with a
  * system-scope release, waits until all ranks' pairs are in its own buffer
  * (at most limit_ns of global time), and adds them in rank order (the same
- * bits on every rank).  On success *status = 0, sumcount = global [sum,
- * count], out[0] = sum / count; on a timeout *status = 1 and out[0] = NaN.
+ * bits on every rank).  On success sumcount = global [sum, count] and out[0]
+ * = sum / count.  *status (zeroed once at set-up) is sticky: a wait that
+ * runs out sets 1, a peer flag above this rank's epoch (a peer that gave up
+ * waiting and stepped on) sets 2, out[0] is then NaN, and every later call
+ * with a nonzero status returns NaN at once without writing to any peer.
  * Replaces ouroboros/specs.py's per-row cross-entropy (:239-241) reduced to
  * the mean over valid rows with the rows sharded across GPUs; the reference
  * has no multi-GPU path. */
@@ -220,6 +223,16 @@ int b2k_ce_reduce_exchange_mean(const float* row_loss, const int64_t* tgt, int64
                                 int64_t ignore_index, void* const* peers, int rank, int world,
                                 unsigned long long limit_ns, double* sumcount, float* out,
                                 int* status, void* stream);
+
+/* The exchange of b2k_ce_reduce_exchange_mean alone: global[0..1] = the sum
+ * over all ranks of local[0..1] (two device doubles per rank), added in rank
+ * order, through the same buffers and epoch sequence (every rank makes the
+ * same sequence of exchange calls).  NaN and a sticky *status on a failure,
+ * as above.  Used for the global valid count that scales the fused
+ * cross-entropy gradient when the rows are sharded; no reference
+ * counterpart (the reference has no multi-GPU path). */
+int b2k_exchange_pair(const double* local, void* const* peers, int rank, int world,
+                      unsigned long long limit_ns, double* global, int* status, void* stream);
 
 /* Exchange-buffer plumbing (no reference counterpart): a zeroed device
  * allocation of b2k_ce_exchange_bytes(world) bytes on the current device, its

@@ -63,6 +63,8 @@ SIGNATURES = {
     "b2k_ce_reduce_exchange_mean": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int,
                                             c_int, ctypes.c_ulonglong, c_void_p, c_void_p,
                                             c_void_p, c_void_p]),
+    "b2k_exchange_pair": (c_int, [c_void_p, c_void_p, c_int, c_int, ctypes.c_ulonglong,
+                                  c_void_p, c_void_p, c_void_p]),
     "b2k_ce_valid_count": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
     "b2k_cross_entropy_fwd_bwd": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int,
                                           c_int64, c_void_p, c_float, c_void_p, c_void_p,

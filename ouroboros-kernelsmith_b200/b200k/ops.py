@@ -562,10 +562,11 @@ def cross_entropy_fwd_bwd(logits, tgt, ignore_index: int = -100, group=None,
     in one pass over the logits: returns (loss 0-dim fp32, dlogits) with
     dlogits = grad_scale * d(mean loss)/d logits in the logits' dtype
     (0 for ignored rows).  With a process group, logits/tgt are this rank's
-    row shard; the valid count and the loss sum are all-reduced (NCCL) so
-    the loss and gradient are those of the global mean.  inplace=True writes
+    row shard; the valid count and the loss sum are summed over the ranks
+    (over peer memory where the exchange is set up, else NCCL all-reduces)
+    so the loss and gradient are those of the global mean.  inplace=True writes
     the gradient over the logits (the memory-saving form of fused CE)."""
-    from .dist import allreduce_sumcount
+    from .dist import XCHG_LIMIT_NS, allreduce_sumcount, ce_exchange
     dev = _cuda(logits, tgt)
     dt = _dtype_id(logits)
     n = logits.shape[-1]
@@ -580,15 +581,34 @@ def cross_entropy_fwd_bwd(logits, tgt, ignore_index: int = -100, group=None,
     row_loss = torch.empty((m,), dtype=torch.float32, device=dev)
     sumcount = torch.empty((2,), dtype=torch.float64, device=dev)
     out = torch.empty((), dtype=torch.float32, device=dev)
+    xchg = ce_exchange(group, dev)
     with _dev(dev) as stream:
         L.check(L.lib.b2k_ce_valid_count(_p(t1), m, ignore_index, _p(count), stream),
                 "b2k_ce_valid_count")
     count[1:].zero_()
-    allreduce_sumcount(count, group)
+    if xchg is not None:
+        # the global valid count and, after the kernel, the loss sum: both
+        # over peer memory (no collective library on the step)
+        xchg.raise_if_failed()
+        count_g = torch.empty((2,), dtype=torch.float64, device=dev)
+        with _dev(dev) as stream:
+            L.check(L.lib.b2k_exchange_pair(_p(count), _p(xchg.peers), xchg.rank, xchg.world,
+                                            XCHG_LIMIT_NS, _p(count_g), _p(xchg.status), stream),
+                    "b2k_exchange_pair")
+        count = count_g
+    else:
+        allreduce_sumcount(count, group)
     with _dev(dev) as stream:
         L.check(L.lib.b2k_cross_entropy_fwd_bwd(_p(x2), ldx, _p(t1), m, n, dt, ignore_index,
                                                 _p(count), grad_scale, _p(row_loss), _p(dx),
                                                 lddx, stream), "b2k_cross_entropy_fwd_bwd")
+        if xchg is not None:
+            L.check(L.lib.b2k_ce_reduce_exchange_mean(
+                _p(row_loss), _p(t1), m, ignore_index, _p(xchg.peers), xchg.rank, xchg.world,
+                XCHG_LIMIT_NS, _p(sumcount), _p(out), _p(xchg.status), stream),
+                "b2k_ce_reduce_exchange_mean")
+            xchg.after_launch()
+            return out, dx.view(logits.shape)
         L.check(L.lib.b2k_ce_reduce(_p(row_loss), _p(t1), m, ignore_index, _p(sumcount), stream),
                 "b2k_ce_reduce")
     allreduce_sumcount(sumcount, group)

@@ -57,17 +57,97 @@ __host__ __device__ constexpr size_t xchg_epoch_off(int world) {
 }
 __host__ __device__ constexpr size_t xchg_bytes(int world) { return xchg_epoch_off(world) + 8; }
 
+// The exchange of one [sum, count] pair: every rank stores (ts, tc) into its
+// slot in every rank's buffer and publishes it; each rank then waits
+// (bounded) for all flags of the epoch in its own buffer and adds the pairs in
+// rank order.  Called by every thread of the block (barriers inside); thread
+// 0 holds (ts, tc) on entry and (S, C) on a true return.  False when a wait ran
+// out or a peer ran ahead: *status is then set (sticky) and nothing more is
+// read.
+struct XchgShared {
+  int timed_out, ran_ahead;
+  unsigned long long epoch;
+};
+
+__device__ __forceinline__ bool exchange_pair(double ts, double tc, unsigned char* const* peers,
+                                              int rank, int world,
+                                              unsigned long long limit_ns, int* status,
+                                              XchgShared& sh, double& S, double& C) {
+  unsigned char* mine = peers[rank];
+  if (threadIdx.x == 0) {
+    sh.timed_out = 0;
+    sh.ran_ahead = 0;
+    unsigned long long* ep = reinterpret_cast<unsigned long long*>(mine + xchg_epoch_off(world));
+    const unsigned long long epoch = *ep + 1;
+    *ep = epoch;
+    sh.epoch = epoch;
+    const int par = (int)(epoch & 1);
+    for (int r = 0; r < world; ++r) {
+      unsigned char* base = peers[r];
+      double* pair = reinterpret_cast<double*>(base + xchg_pair_off(par, world, rank));
+      pair[0] = ts;
+      pair[1] = tc;
+      // release: the pair is visible to whoever acquires the flag
+      st_release_sys_u64(reinterpret_cast<unsigned long long*>(base + xchg_flag_off(par, world, rank)),
+                         epoch);
+    }
+  }
+  __syncthreads();
+  const unsigned long long epoch = sh.epoch;
+  const int par = (int)(epoch & 1);
+  // thread r watches rank r's flag in this rank's own buffer, bounded
+  if (threadIdx.x < world) {
+    const unsigned long long* flag =
+        reinterpret_cast<const unsigned long long*>(mine + xchg_flag_off(par, world, threadIdx.x));
+    unsigned long long f = ld_acquire_sys_u64(flag);
+    if (f < epoch) {
+      const unsigned long long t0 = globaltimer();
+      for (uint32_t i = 1;; ++i) {
+        f = ld_acquire_sys_u64(flag);
+        if (f >= epoch) break;
+        if ((i & 63u) == 0 && globaltimer() - t0 > limit_ns) {
+          atomicExch(&sh.timed_out, 1);
+          break;
+        }
+      }
+    }
+    if (f > epoch) atomicExch(&sh.ran_ahead, 1);  // a peer two calls ahead: see above
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return true;
+  if (sh.timed_out || sh.ran_ahead) {
+    atomicAdd(&b2k_tu_timeouts, 1u);
+    *status = sh.ran_ahead ? 2 : 1;
+    return false;
+  }
+  S = 0.0;
+  C = 0.0;
+  for (int r = 0; r < world; ++r) {
+    // acquire again in this thread, then read past the L1 (cache-volatile)
+    (void)ld_acquire_sys_u64(
+        reinterpret_cast<const unsigned long long*>(mine + xchg_flag_off(par, world, r)));
+    const double* pair = reinterpret_cast<const double*>(mine + xchg_pair_off(par, world, r));
+    S += __ldcv(pair);
+    C += __ldcv(pair + 1);
+  }
+  return true;
+}
+
+__device__ __forceinline__ bool exchange_failed_before(const int* status) {
+  return *reinterpret_cast<const volatile int*>(status) != 0;
+}
+
 __global__ void __launch_bounds__(1024) ce_reduce_exchange_mean_kernel(
     const float* loss, const int64_t* tgt, int64_t M, int64_t ignore,
     unsigned char* const* peers, int rank, int world, unsigned long long limit_ns,
     double* sumcount, float* out, int* status) {
   __shared__ double rs[32], rc[32];
-  __shared__ int timed_out, ran_ahead;
-  __shared__ unsigned long long epoch_s;
+  __shared__ XchgShared sh;
+  const double qnan = __longlong_as_double(0x7ff8000000000000ll);
   // a failed exchange stays failed (sticky status): no pair is published
-  if (*reinterpret_cast<volatile int*>(status) != 0) {
+  if (exchange_failed_before(status)) {
     if (threadIdx.x == 0) {
-      sumcount[0] = __longlong_as_double(0x7ff8000000000000ll);
+      sumcount[0] = qnan;
       sumcount[1] = 0.0;
       out[0] = __int_as_float(0x7fc00000);
     }
@@ -83,70 +163,37 @@ __global__ void __launch_bounds__(1024) ce_reduce_exchange_mean_kernel(
     c += __shfl_xor_sync(0xffffffffu, c, o);
   }
   if ((threadIdx.x & 31) == 0) { rs[threadIdx.x >> 5] = s; rc[threadIdx.x >> 5] = c; }
-  if (threadIdx.x == 0) { timed_out = 0; ran_ahead = 0; }
   __syncthreads();
-  unsigned char* mine = peers[rank];
-  if (threadIdx.x == 0) {
-    double ts = 0.0, tc = 0.0;
+  double ts = 0.0, tc = 0.0;
+  if (threadIdx.x == 0)
     for (int i = 0; i < (int)(blockDim.x >> 5); ++i) { ts += rs[i]; tc += rc[i]; }
-    unsigned long long* ep = reinterpret_cast<unsigned long long*>(mine + xchg_epoch_off(world));
-    const unsigned long long epoch = *ep + 1;
-    *ep = epoch;
-    epoch_s = epoch;
-    const int par = (int)(epoch & 1);
-    for (int r = 0; r < world; ++r) {
-      unsigned char* base = peers[r];
-      double* pair = reinterpret_cast<double*>(base + xchg_pair_off(par, world, rank));
-      pair[0] = ts;
-      pair[1] = tc;
-      // release: the pair is visible to whoever acquires the flag
-      st_release_sys_u64(reinterpret_cast<unsigned long long*>(base + xchg_flag_off(par, world, rank)),
-                         epoch);
-    }
-  }
-  __syncthreads();
-  const unsigned long long epoch = epoch_s;
-  const int par = (int)(epoch & 1);
-  // thread r watches rank r's flag in this rank's own buffer, bounded
-  if (threadIdx.x < world) {
-    const unsigned long long* flag =
-        reinterpret_cast<const unsigned long long*>(mine + xchg_flag_off(par, world, threadIdx.x));
-    unsigned long long f = ld_acquire_sys_u64(flag);
-    if (f < epoch) {
-      const unsigned long long t0 = globaltimer();
-      for (uint32_t i = 1;; ++i) {
-        f = ld_acquire_sys_u64(flag);
-        if (f >= epoch) break;
-        if ((i & 63u) == 0 && globaltimer() - t0 > limit_ns) {
-          atomicExch(&timed_out, 1);
-          break;
-        }
-      }
-    }
-    if (f > epoch) atomicExch(&ran_ahead, 1);  // a peer two calls ahead: see above
-  }
-  __syncthreads();
+  double S = 0.0, C = 0.0;
+  const bool ok = exchange_pair(ts, tc, peers, rank, world, limit_ns, status, sh, S, C);
   if (threadIdx.x == 0) {
-    if (timed_out || ran_ahead) {
-      atomicAdd(&b2k_tu_timeouts, 1u);
-      *status = ran_ahead ? 2 : 1;
-      sumcount[0] = __longlong_as_double(0x7ff8000000000000ll);
-      sumcount[1] = 0.0;
-      out[0] = __int_as_float(0x7fc00000);
-    } else {
-      double S = 0.0, C = 0.0;
-      for (int r = 0; r < world; ++r) {
-        // acquire again in this thread, then read past the L1 (cache-volatile)
-        (void)ld_acquire_sys_u64(
-            reinterpret_cast<const unsigned long long*>(mine + xchg_flag_off(par, world, r)));
-        const double* pair = reinterpret_cast<const double*>(mine + xchg_pair_off(par, world, r));
-        S += __ldcv(pair);
-        C += __ldcv(pair + 1);
-      }
-      sumcount[0] = S;
-      sumcount[1] = C;
-      out[0] = (float)(S / C);  // 0/0 -> NaN (no valid row anywhere)
-    }
+    sumcount[0] = ok ? S : qnan;
+    sumcount[1] = ok ? C : 0.0;
+    out[0] = ok ? (float)(S / C) : __int_as_float(0x7fc00000);  // 0/0 -> NaN: no valid row
+  }
+}
+
+// The pair exchange alone: global = the sum over all ranks of local (two
+// doubles in device memory).  NaN on a failure (sticky, as above).
+__global__ void __launch_bounds__(32) exchange_pair_kernel(const double* local,
+                                                           unsigned char* const* peers, int rank,
+                                                           int world, unsigned long long limit_ns,
+                                                           double* global, int* status) {
+  __shared__ XchgShared sh;
+  const double qnan = __longlong_as_double(0x7ff8000000000000ll);
+  if (exchange_failed_before(status)) {
+    if (threadIdx.x == 0) { global[0] = qnan; global[1] = qnan; }
+    return;
+  }
+  const double ts = threadIdx.x == 0 ? local[0] : 0.0, tc = threadIdx.x == 0 ? local[1] : 0.0;
+  double S = 0.0, C = 0.0;
+  const bool ok = exchange_pair(ts, tc, peers, rank, world, limit_ns, status, sh, S, C);
+  if (threadIdx.x == 0) {
+    global[0] = ok ? S : qnan;
+    global[1] = ok ? C : qnan;
   }
 }
 
@@ -177,6 +224,20 @@ extern "C" int b2k_ce_reduce_exchange_mean(const float* row_loss, const int64_t*
       row_loss, tgt, M, ignore_index, reinterpret_cast<unsigned char* const*>(peers), rank, world,
       limit_ns, sumcount, out, status);
   return b2k::check_launch("b2k_ce_reduce_exchange_mean");
+}
+
+extern "C" int b2k_exchange_pair(const double* local, void* const* peers, int rank, int world,
+                                 unsigned long long limit_ns, double* global, int* status,
+                                 void* stream) {
+  B2K_REQUIRE(world >= 1 && world <= 32 && rank >= 0 && rank < world,
+              "b2k_exchange_pair: rank %d of world %d", rank, world);
+  B2K_REQUIRE(local != nullptr && peers != nullptr && global != nullptr && status != nullptr,
+              "b2k_exchange_pair: null pointer");
+  B2K_REQUIRE(limit_ns > 0 && limit_ns <= 10000000000ull,
+              "b2k_exchange_pair: wait limit outside (0, 10 s]");
+  b2k::exchange_pair_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      local, reinterpret_cast<unsigned char* const*>(peers), rank, world, limit_ns, global, status);
+  return b2k::check_launch("b2k_exchange_pair");
 }
 
 // ---------------------------------------------------------------------------

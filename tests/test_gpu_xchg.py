@@ -86,6 +86,23 @@ def test_missing_rank_times_out_and_context_survives():
     assert _lib.lib.b2k_pipeline_timeouts(1) == 0
 
 
+def test_single_rank_pair_exchange_returns_the_pair():
+    """b2k_exchange_pair with one rank: the global pair is the local one, over
+    several calls (both slot parities), status 0."""
+    buf = torch.zeros(int(_lib.lib.b2k_ce_exchange_bytes(1)), dtype=torch.uint8, device="cuda")
+    peers = torch.tensor([buf.data_ptr()], dtype=torch.int64, device="cuda")
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    for k in range(3):
+        local = torch.tensor([1234.5 + k, 7.0 * k], dtype=torch.float64, device="cuda")
+        glob = torch.empty(2, dtype=torch.float64, device="cuda")
+        st = _lib.lib.b2k_exchange_pair(local.data_ptr(), peers.data_ptr(), 0, 1, 1_000_000_000,
+                                        glob.data_ptr(), status.data_ptr(),
+                                        torch.cuda.current_stream().cuda_stream)
+        assert st == _lib.OK, _lib.last_error()
+        torch.cuda.synchronize()
+        assert torch.equal(glob, local) and int(status.item()) == 0
+
+
 def test_failed_exchange_stays_failed_and_writes_nothing():
     """After a wait ran out, the status word is sticky: the next call with it
     returns NaN at once, publishes nothing into any buffer and leaves the
@@ -149,7 +166,9 @@ def _rank_main(rank, world, port, q):
         r0, r1 = bd.shard_rows(M, rank, world)
         outs = [float(b200k.cross_entropy_mean(x[r0:r1], t[r0:r1])) for _ in range(5)]
         used = bd.ce_exchange(None, torch.device("cuda", rank)) is not None
-        q.put((rank, outs, used))
+        # the fused loss + gradient: valid count and loss sum over peer memory
+        loss, dx = b200k.cross_entropy_fwd_bwd(x[r0:r1], t[r0:r1])
+        q.put((rank, outs, used, float(loss), dx.float().cpu()))
         torch.cuda.synchronize()
         dist.barrier()
         bd.close_exchanges()
@@ -177,10 +196,18 @@ def test_two_ranks_match_one_gpu():
     t = torch.randint(0, V, (M,), generator=g, device="cuda")
     t[::7] = -100
     ref = float(b200k.cross_entropy_mean(x, t))
-    for rank, outs, used in res:
+    ref_loss, ref_dx = b200k.cross_entropy_fwd_bwd(x, t)
+    ref_dx = ref_dx.float().cpu()
+    res.sort(key=lambda r: r[0])
+    for rank, outs, used, loss, dx in res:
         assert used, f"rank {rank} did not use the peer-memory exchange"
         assert all(o == outs[0] for o in outs)
         # the row losses are the same; sums of two fp64 halves vs one pass may
         # differ in the last bits of the fp64 sum, not in the fp32 mean
         assert abs(outs[0] - ref) <= 1e-6 * abs(ref), (outs[0], ref)
+        assert abs(loss - float(ref_loss)) <= 1e-6 * abs(float(ref_loss)), (loss, float(ref_loss))
+        r0, r1 = (0, 2001) if rank == 0 else (2001, 4001)
+        # the same global valid count scales every rank's rows: equal bits
+        assert torch.equal(dx, ref_dx[r0:r1]), f"rank {rank}: gradient differs"
     assert res[0][1][0] == res[1][1][0]  # every rank gets the same bits
+    assert res[0][3] == res[1][3]
