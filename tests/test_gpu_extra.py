@@ -284,8 +284,8 @@ def test_two_devices_in_one_process():
 @pytest.mark.parametrize("M", [3, 700, 2000, 8000])
 def test_cross_entropy_few_rows_per_block(dt, M):
     """Vocabulary-length rows with few rows per resident block (a shard of
-    the logits on one of many GPUs; the grid is balanced so every block walks
-    the same number of rows).  Sampled rows against the oracle, including
+    the logits on one of many GPUs, so the last round of rows leaves most
+    blocks idle).  Sampled rows against the oracle, including
     ignored rows, a bad target (NaN) and targets in the first and last chunk
     of a row, plus the mean over all rows."""
     V = 128256
@@ -316,6 +316,37 @@ def test_cross_entropy_few_rows_per_block(dt, M):
                                                      ignore_index=-100, reduction="sum"))
         c += int((t[r:r + 1024] != -100).sum())
     assert abs(got - s / c) <= 1e-3 * abs(s / c), (got, s / c)
+
+
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("M,N,pad", [(1500, 1024, 0), (3000, 4096, 0), (5000, 2048, 64),
+                                     (1300, 8192, 0), (2400, 1032, 8), (160000, 1024, 0)])
+def test_cross_entropy_many_short_rows(dt, M, N, pad):
+    """Many rows of 2..16 KB (the warp-per-row ring), strided rows among them,
+    and 160000 rows so that each warp walks more than 64 rows (its window of
+    read-ahead targets slides).  Ignored rows and out-of-range targets are
+    never copied: 0 and NaN.  All rows against the fp32 torch expression,
+    sampled rows against the oracle."""
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    base = (torch.randn((M, N + pad), generator=g, device="cuda") * 4).to(TDT[dt])
+    x = base[:, :N]
+    t = torch.randint(0, N, (M,), generator=g, device="cuda")
+    t[::13] = -100
+    t[0] = 0
+    t[1] = N - 1
+    t[5::97] = N + 3  # outside [0, N): NaN
+    t[7::101] = -7
+    out = b200k.cross_entropy(x, t)
+    bad = (t != -100) & ((t < 0) | (t >= N))
+    assert torch.isnan(out[bad]).all().item()
+    ok = ~bad
+    xf = x.float()
+    ref = torch.logsumexp(xf, dim=1) - xf.gather(1, t.clamp(0, N - 1)[:, None])[:, 0]
+    ref = torch.where(t == -100, torch.zeros_like(ref), ref)
+    _close(out[ok].float(), ref[ok].to(TDT[dt]).float().cpu().numpy(), dt)
+    rows = np.arange(0, M, max(1, M // 29))
+    rows = rows[ok.cpu().numpy()[rows]]
+    _close(out[rows], O.cross_entropy(x[rows].float().cpu().numpy(), t[rows].cpu().numpy(), dt), dt)
 
 
 @pytest.mark.parametrize("dt", DTS)
