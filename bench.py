@@ -245,7 +245,27 @@ class Workload:
     def expr(self, *inputs): ...
 
     def e2e_api(self):
-        return "b200k.host.run_rows_host (pinned host buffers, copies overlapped with kernels)"
+        return ("b200k.host.RowsHostGraph (pinned host buffers; each run replays the "
+                "host->device copies, the kernels and the device->host copies of every "
+                f"{self.host_graph.chunk_rows}-row chunk, overlapped on three streams)")
+
+    def _host_graph(self, fn, row_inputs, other_inputs, out):
+        from b200k.host import RowsHostGraph
+        self.host_graph = RowsHostGraph(fn, row_inputs, other_inputs, out=out,
+                                        device=self.device)
+
+    def e2e_step(self, timing):
+        self.host_graph.run(timing)
+
+    def e2e_verify(self):
+        """The host outputs of the last end-to-end run against the device op on
+        the same inputs (the device op's launch may differ by chunk size, so
+        at the spec tolerance of the output dtype)."""
+        want = self.run(*self.sets[0])
+        want = tuple(want) if isinstance(want, (tuple, list)) else (want,)
+        got = self.host_graph.out
+        got = tuple(got) if isinstance(got, (tuple, list)) else (got,)
+        return all(_close(g.to(self.device), w, w.dtype)[0] for g, w in zip(got, want))
 
 
 class Chain(Workload):
@@ -294,17 +314,14 @@ class Chain(Workload):
     def e2e_setup(self):
         x, r = self.sets[0]
         self.hx, self.hr = x.cpu().pin_memory(), r.cpu().pin_memory()
-        self.hw, self.hb = self.w.cpu(), self.b.cpu()
+        self.hw, self.hb = self.w.cpu().pin_memory(), self.b.cpu().pin_memory()
         self.hh = torch.empty_like(self.hx).pin_memory()
         self.hy = torch.empty_like(self.hx).pin_memory()
-        return (2 * self.rows * self.N * 2 + 2 * self.N * 2, 2 * self.rows * self.N * 2)
-
-    def e2e_step(self, timing):
-        from b200k.host import run_rows_host
         b2k = self.b2k
-        run_rows_host(lambda x, r, w, b: b2k.fused_add_norm(x, r, w, b, norm="layer", act="gelu"),
-                      [self.hx, self.hr], [self.hw, self.hb], out=(self.hh, self.hy),
-                      device=self.device, timing=timing)
+        self._host_graph(lambda x, r, w, b: b2k.fused_add_norm(x, r, w, b, norm="layer",
+                                                               act="gelu"),
+                         [self.hx, self.hr], [self.hw, self.hb], (self.hh, self.hy))
+        return (2 * self.rows * self.N * 2 + 2 * self.N * 2, 2 * self.rows * self.N * 2)
 
     # CPU: oracle restatement of the same chain on float32 values
     def cpu_prepare(self):
@@ -356,14 +373,10 @@ class RMSNorm(Workload):
 
     def e2e_setup(self):
         self.hx = self.sets[0][0].cpu().pin_memory()
-        self.hw = self.w.cpu()
+        self.hw = self.w.cpu().pin_memory()
         self.hy = torch.empty_like(self.hx).pin_memory()
+        self._host_graph(self.b2k.rmsnorm, [self.hx], [self.hw], self.hy)
         return (self.rows * self.N * 2 + self.N * 2, self.rows * self.N * 2)
-
-    def e2e_step(self, timing):
-        from b200k.host import run_rows_host
-        run_rows_host(self.b2k.rmsnorm, [self.hx], [self.hw], out=self.hy, device=self.device,
-                      timing=timing)
 
     def cpu_prepare(self):
         from oracle.numerics import f16_round
@@ -406,12 +419,8 @@ class SwiGLU(Workload):
         g, u = self.sets[0]
         self.hg, self.hu = g.cpu().pin_memory(), u.cpu().pin_memory()
         self.hy = torch.empty_like(self.hg).pin_memory()
+        self._host_graph(self.b2k.swiglu, [self.hg, self.hu], [], self.hy)
         return (2 * self.rows * self.N * 2, self.rows * self.N * 2)
-
-    def e2e_step(self, timing):
-        from b200k.host import run_rows_host
-        run_rows_host(self.b2k.swiglu, [self.hg, self.hu], [], out=self.hy, device=self.device,
-                      timing=timing)
 
     def cpu_prepare(self):
         from oracle.numerics import bf16_round
@@ -698,18 +707,14 @@ class RoPE(Workload):
     def e2e_setup(self):
         q, k = self.sets[0]
         self.hq, self.hk = q.cpu().pin_memory(), k.cpu().pin_memory()
-        self.hc, self.hs = self.cos.cpu(), self.sin.cpu()
+        self.hc, self.hs = self.cos.cpu().pin_memory(), self.sin.cpu().pin_memory()
         self.hqo = torch.empty_like(self.hq).pin_memory()
         self.hko = torch.empty_like(self.hk).pin_memory()
+        b2k, inter = self.b2k, self.interleaved
+        self._host_graph(lambda q, k, c, s: b2k.rope_qk(q, k, c, s, interleaved=inter),
+                         [self.hq, self.hk], [self.hc, self.hs], (self.hqo, self.hko))
         qk = (self.rows * self.S * (self.H + self.Hk) * self.D) * 2
         return (qk + 2 * self.S * (self.D // 2) * 2, qk)
-
-    def e2e_step(self, timing):
-        from b200k.host import run_rows_host
-        b2k, inter = self.b2k, self.interleaved
-        run_rows_host(lambda q, k, c, s: b2k.rope_qk(q, k, c, s, interleaved=inter),
-                      [self.hq, self.hk], [self.hc, self.hs], out=(self.hqo, self.hko),
-                      device=self.device, timing=timing)
 
     def cpu_prepare(self):
         from oracle.numerics import bf16_round
@@ -1381,6 +1386,9 @@ def main():
         e2e = {"value": round(e_total / (e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                "ms_per_step": round(e_ms, 4), "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "api": wl.e2e_api()}
+        if hasattr(wl, "host_graph"):
+            e2e["parity"] = all(ranks.gather(1.0 if wl.e2e_verify() else 0.0))
+            del wl.host_graph  # releases the captured pipeline's device buffers
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
