@@ -292,6 +292,13 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_rows_kernel(const NormAr
   const bool valid = row < a.M;
   const int N = (int)a.N;
   const bool aligned = a.aligned;
+  {
+    const int64_t row0 = (int64_t)blockIdx.x * blockDim.y;
+    const int64_t nr = a.M - row0 < (int64_t)blockDim.y ? a.M - row0 : (int64_t)blockDim.y;
+    pdl_rows_prologue(a.x, a.ldx * (int64_t)sizeof(T), RESID ? a.r : nullptr,
+                      a.ldr * (int64_t)sizeof(T), row0, nr, (uint32_t)N * (uint32_t)sizeof(T),
+                      aligned && a.l2_prefetch_rows > 0);
+  }
   const T* xr = static_cast<const T*>(a.x) + (valid ? row * a.ldx : 0);
   const T* rr = RESID ? static_cast<const T*>(a.r) + (valid ? row * a.ldr : 0) : nullptr;
 
@@ -741,9 +748,9 @@ static int norm_launch_resid(const NormArgs& a, cudaStream_t st) {
     const dim3 block(cfg.G, cfg.R);
     const int64_t grid = (a.M + cfg.R - 1) / cfg.R;
     switch (cfg.V) {
-      case 1: norm_rows_kernel<T, 1, RESID, MODE, ACT><<<grid, block, 0, st>>>(a); break;
-      case 2: norm_rows_kernel<T, 2, RESID, MODE, ACT><<<grid, block, 0, st>>>(a); break;
-      default: norm_rows_kernel<T, 4, RESID, MODE, ACT><<<grid, block, 0, st>>>(a); break;
+      case 1: launch_pdl(norm_rows_kernel<T, 1, RESID, MODE, ACT>, dim3((unsigned)grid), block, 0, st, a); break;
+      case 2: launch_pdl(norm_rows_kernel<T, 2, RESID, MODE, ACT>, dim3((unsigned)grid), block, 0, st, a); break;
+      default: launch_pdl(norm_rows_kernel<T, 4, RESID, MODE, ACT>, dim3((unsigned)grid), block, 0, st, a); break;
     }
   } else {
     norm_rows_stream_kernel<T, RESID, MODE, ACT><<<a.M, dim3(kNormMaxThreads, 1), 0, st>>>(a);

@@ -40,6 +40,13 @@ __global__ void __launch_bounds__(kRedMaxThreads) entropy_rows_kernel(const RowR
   const Group g;
   const int64_t row = (int64_t)blockIdx.x * blockDim.y + g.ty;
   const bool valid = row < a.M;
+  {
+    const int64_t row0 = (int64_t)blockIdx.x * blockDim.y;
+    const int64_t nr = a.M - row0 < (int64_t)blockDim.y ? a.M - row0 : (int64_t)blockDim.y;
+    pdl_rows_prologue(a.x, a.ldx * (int64_t)sizeof(T), nullptr,
+                      a.ldy * (int64_t)sizeof(T), row0, nr, (uint32_t)a.N * (uint32_t)sizeof(T),
+                      a.aligned && a.l2pf_rows > 0);
+  }
   const int N = valid ? a.N : 0;
   const T* xr = static_cast<const T*>(a.x) + (valid ? row * a.ldx : 0);
   float xv[V][E];
@@ -82,6 +89,13 @@ __global__ void __launch_bounds__(kRedMaxThreads) kl_rows_kernel(const RowRedArg
   const Group g;
   const int64_t row = (int64_t)blockIdx.x * blockDim.y + g.ty;
   const bool valid = row < a.M;
+  {
+    const int64_t row0 = (int64_t)blockIdx.x * blockDim.y;
+    const int64_t nr = a.M - row0 < (int64_t)blockDim.y ? a.M - row0 : (int64_t)blockDim.y;
+    pdl_rows_prologue(a.x, a.ldx * (int64_t)sizeof(T), a.y,
+                      a.ldy * (int64_t)sizeof(T), row0, nr, (uint32_t)a.N * (uint32_t)sizeof(T),
+                      a.aligned && a.l2pf_rows > 0);
+  }
   const int N = valid ? a.N : 0;
   const T* xr = static_cast<const T*>(a.x) + (valid ? row * a.ldx : 0);
   const T* yr = static_cast<const T*>(a.y) + (valid ? row * a.ldy : 0);
@@ -239,6 +253,12 @@ __global__ void __launch_bounds__(kRedMaxThreads) cumsum_kernel(const RowRedArgs
   const Group g;
   const int64_t row = (int64_t)blockIdx.x * blockDim.y + g.ty;
   const bool valid = row < a.M;
+  {
+    const int64_t row0 = (int64_t)blockIdx.x * blockDim.y;
+    const int64_t nr = a.M - row0 < (int64_t)blockDim.y ? a.M - row0 : (int64_t)blockDim.y;
+    pdl_rows_prologue(a.x, a.ldx * (int64_t)sizeof(T), nullptr, 0, row0, nr,
+                      (uint32_t)a.N * (uint32_t)sizeof(T), a.aligned && a.l2pf_rows > 0);
+  }
   const int N = valid ? a.N : 0;
   const int nN = a.N;
   const T* xr = static_cast<const T*>(a.x) + (valid ? row * a.ldx : 0);
@@ -665,7 +685,7 @@ static int rowred_launch(const RowRedArgs& a, bool kl, cudaStream_t st) {
   if (choose_row_cfg(a.N, E, 128, &cfg, 4, kRedMaxThreads)) {
     const dim3 block(cfg.G, cfg.R);
     const int64_t grid = (a.M + cfg.R - 1) / cfg.R;
-    auto go = [&](auto kern) { kern<<<(unsigned)grid, block, 0, st>>>(a); };
+    auto go = [&](auto kern) { launch_pdl(kern, dim3((unsigned)grid), block, 0, st, a); };
     if (kl) {
       switch (cfg.V) {
         case 1: go(kl_rows_kernel<T, 1>); break;
@@ -695,7 +715,7 @@ static int cumsum_launch(const RowRedArgs& a, cudaStream_t st) {
   G = G < 1 ? 1 : (G > 256 ? 256 : G);
   const int R = G >= 256 ? 1 : 256 / G;
   const int64_t grid = (a.M + R - 1) / R;
-  cumsum_kernel<T><<<(unsigned)grid, dim3(G, R), 0, st>>>(a);
+  launch_pdl(cumsum_kernel<T>, dim3((unsigned)grid), dim3(G, R), 0, st, a);
   return check_launch("b2k_cumsum");
 }
 

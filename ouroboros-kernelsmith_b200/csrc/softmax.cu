@@ -140,6 +140,12 @@ __global__ void __launch_bounds__(kSmMaxThreads) softmax_rows_kernel(const Softm
   const bool valid = row < a.M;
   const int N = a.N;
   const bool aligned = a.aligned;
+  {
+    const int64_t row0 = (int64_t)blockIdx.x * blockDim.y;
+    const int64_t nr = a.M - row0 < (int64_t)blockDim.y ? a.M - row0 : (int64_t)blockDim.y;
+    pdl_rows_prologue(a.x, a.ldx * (int64_t)sizeof(T), nullptr, 0, row0, nr,
+                      (uint32_t)N * (uint32_t)sizeof(T), aligned && a.l2pf_rows > 0);
+  }
   const float scale = (KIND == B2K_SOFTMAX_SCALE) ? load_scalar(a.scale, a.scale_dtype) : 1.0f;
   const T* xr = static_cast<const T*>(a.x) + (valid ? row * a.ldx : 0);
   float2 hv[V][H];
@@ -308,9 +314,9 @@ static int softmax_launch(const SoftmaxArgs& a, cudaStream_t st) {
     const dim3 block(cfg.G, cfg.R);
     const int64_t grid = (a.M + cfg.R - 1) / cfg.R;
     switch (cfg.V) {
-      case 1: softmax_rows_kernel<T, KIND, 1><<<grid, block, 0, st>>>(a); break;
-      case 2: softmax_rows_kernel<T, KIND, 2><<<grid, block, 0, st>>>(a); break;
-      default: softmax_rows_kernel<T, KIND, 4><<<grid, block, 0, st>>>(a); break;
+      case 1: launch_pdl(softmax_rows_kernel<T, KIND, 1>, dim3((unsigned)grid), block, 0, st, a); break;
+      case 2: launch_pdl(softmax_rows_kernel<T, KIND, 2>, dim3((unsigned)grid), block, 0, st, a); break;
+      default: launch_pdl(softmax_rows_kernel<T, KIND, 4>, dim3((unsigned)grid), block, 0, st, a); break;
     }
   } else {
     softmax_stream_kernel<T, KIND><<<a.M, kSmMaxThreads, 0, st>>>(a);

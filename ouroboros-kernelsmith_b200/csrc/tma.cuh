@@ -193,6 +193,27 @@ __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Prologue of a non-persistent row kernel launched with launch_pdl, whose
+// block handles rows [row0, row0 + nrows) of up to two inputs (x, r; r may be
+// null): lets the next kernel of the stream launch, hints the block's rows
+// into L2 when `hint` (rows 16-byte aligned, a multiple of 16 bytes long) and
+// waits for the previous kernel, before which nothing may be read or written.
+__device__ __forceinline__ void pdl_rows_prologue(const void* x, int64_t ldx_bytes,
+                                                  const void* r, int64_t ldr_bytes,
+                                                  int64_t row0, int64_t nrows,
+                                                  uint32_t row_bytes, bool hint) {
+  griddep_launch_dependents();
+  if (hint && row_bytes > 0 && threadIdx.x == 0 && threadIdx.y == 0) {
+    for (int64_t i = 0; i < nrows; ++i) {
+      bulk_prefetch_l2(static_cast<const unsigned char*>(x) + (row0 + i) * ldx_bytes, row_bytes);
+      if (r)
+        bulk_prefetch_l2(static_cast<const unsigned char*>(r) + (row0 + i) * ldr_bytes,
+                         row_bytes);
+    }
+  }
+  griddep_wait();
+}
+
 // Launch with programmatic dependent launch enabled (B2K_PDL=0 disables it):
 // the kernel's blocks may be scheduled while the previous kernel of the
 // stream drains; the kernel itself calls griddep_wait() before its first

@@ -52,6 +52,10 @@ __global__ void __launch_bounds__(1024) ce_rows_kernel(const CeArgs a) {
   const int64_t row = (int64_t)blockIdx.x * blockDim.y + g.ty;
   const bool valid = row < a.M;
   const int64_t N = a.N;
+  // programmatic dependent launch; no L2 hint, since rows whose target is
+  // ignore_index are not to be read at all
+  griddep_launch_dependents();
+  griddep_wait();
   const int64_t t = valid ? a.tgt[row] : a.ignore;
   const bool ignore = (t == a.ignore);
   const bool bad = !ignore && (t < 0 || t >= N);
@@ -628,7 +632,7 @@ static int ce_launch(const CeArgs& a, cudaStream_t st, bool* bwd_done = nullptr)
   if (override_g) G = override_g;
   const int R = G >= 256 ? 1 : 256 / G;
   const int64_t grid = (a.M + R - 1) / R;
-  ce_rows_kernel<T, OutT><<<(unsigned)grid, dim3(G, R), 0, st>>>(a);
+  launch_pdl(ce_rows_kernel<T, OutT>, dim3((unsigned)grid), dim3(G, R), 0, st, a);
   return check_launch("b2k_cross_entropy");
 }
 
