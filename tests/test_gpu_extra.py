@@ -350,6 +350,35 @@ def test_cross_entropy_many_short_rows(dt, M, N, pad):
 
 
 @pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("op", ["softmax", "softcap_softmax", "log_softmax", "softmax_scale"])
+@pytest.mark.parametrize("M,N,pad", [(3000, 1032, 0), (5000, 2048, 0), (700, 1040, 16),
+                                     (20000, 2048, 0)])
+def test_softmax_family_pipelined_narrow_rows(dt, op, M, N, pad):
+    """Rows of 129..256 16-byte vectors (fp16/bf16 1032..2048 values, fp32
+    1040 and 2048) through the bulk-copy pipeline with 64-thread blocks, many
+    rows per block, strided rows among them: sampled rows against the oracle,
+    every row against the fp32 torch expression."""
+    g = torch.Generator(device="cuda").manual_seed(M + N + pad)
+    base = (torch.randn((M, N + pad), generator=g, device="cuda") * 8).to(TDT[dt])
+    x = base[:, :N]
+    scale = torch.tensor([0.37], device="cuda").to(TDT[dt])
+    fn = getattr(b200k, op)
+    out = fn(x, scale) if op == "softmax_scale" else fn(x)
+    xf = x.float()
+    if op == "softcap_softmax":
+        xf = 30.0 * torch.tanh(xf / 30.0)
+    elif op == "softmax_scale":
+        xf = xf * scale.float()[0]
+    want = torch.log_softmax(xf, -1) if op == "log_softmax" else torch.softmax(xf, -1)
+    _close(out, want.to(TDT[dt]).float().cpu().numpy(), dt)
+    rows = np.arange(0, M, max(1, M // 17))
+    xs = x[rows].float().cpu().numpy()
+    o = getattr(O, op)
+    ref = o(xs, scale.float().cpu().numpy(), dt) if op == "softmax_scale" else o(xs, dt)
+    _close(out[rows], ref, dt)
+
+
+@pytest.mark.parametrize("dt", DTS)
 @pytest.mark.parametrize("op", ["entropy", "kl_div", "cumsum"])
 @pytest.mark.parametrize("shape,scale", [((3000, 1024), 1.0), ((700, 8192), 8.0),
                                          ((333, 4096), 64.0), ((64, 512), 1.0)])
