@@ -1276,6 +1276,18 @@ def run_config(name, wl, args, ranks, stream, local, steps, warmup, peak, world)
              "scaling": wl.scaling, "config": wl.config(), "rows_per_rank": wl.rows,
              "input_sets": wl.nsets, "launch": r["launch"], "steps": steps,
              "gpu_launches": steps * wl.launches_per_step}
+    # what bounds a rank's step when its shard is small: the HBM time of its
+    # bytes at the copy peak against the step it took
+    floor_us = bytes_rank / (peak * 1e9) * 1e6
+    step_us = r["ms_rank"] * 1e3
+    entry["shard"] = {"bytes_per_rank": bytes_rank, "hbm_floor_us": round(floor_us, 3),
+                      "step_us": round(step_us, 3)}
+    if entry["frac"] < 0.9:
+        entry["shard"]["limit"] = (
+            f"{bytes_rank / 1e6:.1f} MB per rank: {floor_us:.2f} us of HBM time at the copy peak "
+            f"inside a {step_us:.2f} us step; the other {step_us - floor_us:.2f} us are the "
+            f"launch, the first rows' loads and the last rows' stores, which do not shrink with "
+            f"the shard")
     if hasattr(wl, "bytes_needed"):
         need = wl.bytes_needed()
         entry["bytes_needed"] = need
@@ -1448,6 +1460,7 @@ def main():
                           "traffic between two uses of a set"),
         "parity": head["parity"], "check": head["check"],
         "per_rank_ms": head["per_rank_ms"], "rows_per_rank": head["rows_per_rank"],
+        "shard": head["shard"],
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_source": peak_kind, "algorithmic_bytes_per_launch": bytes_rank},
