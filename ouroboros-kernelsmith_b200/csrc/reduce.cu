@@ -655,11 +655,12 @@ static bool rowred_try_tma(const RowRedArgs& a, int kind, cudaStream_t st) {
   const int64_t vneed = (nvec + G - 1) / G;
   if (vneed > 4) return false;
   const bool v2 = vneed <= 2;
-  static const int want_stages = [] {
+  static const int stages_knob = [] {
     const char* s = getenv("B2K_TMA_STAGES");
     const int v = s ? atoi(s) : 0;
     return v >= 2 && v <= 8 ? v : 2;
   }();
+  const int want_stages = stages_knob;
   auto go = [&](auto kern, int n_in) -> bool {
     PipeShape ps;
     if (!choose_pipe_shape(kern, G, n_in * row_bytes, 0, want_stages, &ps)) return false;

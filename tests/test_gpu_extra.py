@@ -349,6 +349,33 @@ def test_cross_entropy_many_short_rows(dt, M, N, pad):
     _close(out[rows], O.cross_entropy(x[rows].float().cpu().numpy(), t[rows].cpu().numpy(), dt), dt)
 
 
+@pytest.mark.parametrize("sdt", DTS)
+@pytest.mark.parametrize("M,N", [(3, 48), (1000, 1040), (4096, 4096), (777, 12304), (300000, 16)])
+def test_dequant_flat_rows_bit_exact(sdt, M, N):
+    """The flat vector kernel finds each vector's row by a multiply-high
+    division (1, 3, 65, 256, 769 vectors per row) and builds the int8 values
+    as exact floats: the result must equal (q.float() * scale.float()).half()
+    bit for bit, for fp16, bf16 and fp32 scales."""
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    q = torch.randint(-128, 128, (M, N), generator=g, device="cuda", dtype=torch.int8)
+    sc = (torch.rand((M, 1), generator=g, device="cuda") * 0.05 + 0.001).to(TDT[sdt])
+    sc[::5] = -sc[::5]
+    got = b200k.dequant_int8(q, sc)
+    want = (q.float() * sc.float()).to(torch.float16)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+@pytest.mark.parametrize("dt", DTS)
+@pytest.mark.parametrize("M,N", [(5, 24), (1000, 1032), (3000, 4096)])
+def test_bias_gelu_flat_columns(dt, M, N):
+    """bias_gelu's vector kernel takes each vector's column from the
+    multiply-high division: against the oracle on every row."""
+    x = _randn((M, N), dt, 2.0, M + 1)
+    b = _randn((N,), dt, 0.5, N + 2)
+    got = b200k.bias_gelu(_t(x, dt), _t(b, dt))
+    _close(got, O.bias_gelu(x, b, dt), dt)
+
+
 @pytest.mark.parametrize("dt", DTS)
 @pytest.mark.parametrize("op", ["softmax", "softcap_softmax", "log_softmax", "softmax_scale"])
 @pytest.mark.parametrize("M,N,pad", [(3000, 1032, 0), (5000, 2048, 0), (700, 1040, 16),
