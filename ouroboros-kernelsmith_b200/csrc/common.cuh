@@ -286,6 +286,32 @@ __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2
   m = M;
 }
 
+// cross-warp stage of the group (max, sum-exp) merge (G > 32): warp 0 merges
+// the warps' pairs, every thread gets the result
+__device__ __forceinline__ void group_lse_xwarp(float& m, float& s, const Group& g, float* red) {
+  const int nw = g.G >> 5, w = g.tx >> 5, lane = g.tx & 31;
+  float* rm = red + g.ty * 32;        // [R <= 16][32]
+  float* rs = red + 512 + g.ty * 32;  // (red must hold 1024 floats)
+  if (lane == 0) { rm[w] = m; rs[w] = s; }
+  __syncthreads();
+  if (w == 0) {
+    float M = lane < nw ? rm[lane] : -INFINITY;
+    float S = lane < nw ? rs[lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+      if (o < nw) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, M, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, S, o);
+        lse_merge(M, S, m2, s2);
+      }
+    if (lane == 0) { rm[0] = M; rs[0] = S; }
+  }
+  __syncthreads();
+  m = rm[0];
+  s = rs[0];
+  __syncthreads();
+}
+
 __device__ __forceinline__ void group_lse(float& m, float& s, const Group& g, float* red) {
   const int width = g.G < 32 ? g.G : 32;
 #pragma unroll
@@ -295,29 +321,24 @@ __device__ __forceinline__ void group_lse(float& m, float& s, const Group& g, fl
       const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
       lse_merge(m, s, m2, s2);
     }
-  if (g.G > 32) {
-    const int nw = g.G >> 5, w = g.tx >> 5, lane = g.tx & 31;
-    float* rm = red + g.ty * 32;        // [R <= 16][32]
-    float* rs = red + 512 + g.ty * 32;  // (red must hold 1024 floats)
-    if (lane == 0) { rm[w] = m; rs[w] = s; }
-    __syncthreads();
-    if (w == 0) {
-      float M = lane < nw ? rm[lane] : -INFINITY;
-      float S = lane < nw ? rs[lane] : 0.0f;
+  if (g.G > 32) group_lse_xwarp(m, s, g, red);
+}
+
+// maximum over the warp, in every lane
+__device__ __forceinline__ float warp_allmax(float v) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-        if (o < nw) {
-          const float m2 = __shfl_xor_sync(0xffffffffu, M, o);
-          const float s2 = __shfl_xor_sync(0xffffffffu, S, o);
-          lse_merge(M, S, m2, s2);
-        }
-      if (lane == 0) { rm[0] = M; rs[0] = S; }
-    }
-    __syncthreads();
-    m = rm[0];
-    s = rs[0];
-    __syncthreads();
-  }
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// group_lse for G >= 32 when m is already the same in every lane of a warp
+// (the warp's maximum, taken before the exponentials): the warp stage is a
+// plain sum of s with no exponentials (group_lse's spends two per level),
+// the warps' pairs are merged as in group_lse
+__device__ __forceinline__ void group_lse_wmax(float& m, float& s, const Group& g, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (g.G > 32) group_lse_xwarp(m, s, g, red);
 }
 
 // ---------------------------------------------------------------------------

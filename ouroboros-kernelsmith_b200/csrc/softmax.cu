@@ -61,8 +61,10 @@ struct SoftmaxSlice {
   static constexpr int H = E / 2;
   static constexpr bool P = std::is_same<T, float>::value;
 
-  // transform + local (max, sum-exp); leaves e = exp(t - m_t) in hv for
-  // softmax kinds, t for log-softmax
+  // transform + local (max, sum-exp); leaves e = exp(t - m) in hv for
+  // softmax kinds, t for log-softmax.  m is the thread's maximum, or with WM
+  // the warp's (every lane of the warp calls this; see group_lse_wmax).
+  template <bool WM = false>
   __device__ __forceinline__ static void local(float2 (&hv)[V][H], int N, bool whole,
                                                const Group& g, float scale, float& m,
                                                float& s) {
@@ -79,6 +81,7 @@ struct SoftmaxSlice {
         m = fmaxf(m, fmaxf(t.x, t.y));
       }
     }
+    if constexpr (WM) m = warp_allmax(m);
     s = 0.0f;
     if (m == -INFINITY) return;
     if constexpr (P) {
@@ -207,10 +210,12 @@ __global__ void __launch_bounds__(kSmMaxThreads) softmax_tma_kernel(const Softma
 #pragma unroll
         for (int j = 0; j < H; ++j) hv[v][j] = f2s(0.0f);
     }
+    // the warp's maximum before the exponentials: the warp stage of the
+    // merge is then a plain sum (group_lse_wmax)
     float m, s;
-    Slice::local(hv, N, true, g, scale, m, s);
+    Slice::template local<true>(hv, N, true, g, scale, m, s);
     float M = m, S = s;
-    group_lse(M, S, g, red);
+    group_lse_wmax(M, S, g, red);
     if (abort_flag) break;
     pipe.refill();
     Slice::finish(hv, m, M, S);

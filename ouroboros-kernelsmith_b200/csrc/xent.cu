@@ -509,6 +509,9 @@ __global__ void __launch_bounds__(512) ce_pipe_kernel(const CeArgs a, const int 
 #pragma unroll
         for (int j = 0; j < H; ++j) bm = fmaxf(bm, fmaxf(v[q][j].x, v[q][j].y));
       }
+      // the warp's maximum (the row's branch is the same in the whole block):
+      // the warp stage of the merge is then a plain sum
+      bm = warp_allmax(bm);
       if (bm != -INFINITY) {
         m = bm;
         if constexpr (P) {
@@ -531,7 +534,7 @@ __global__ void __launch_bounds__(512) ce_pipe_kernel(const CeArgs a, const int 
       }
       if (g.tx == 0) xt_s = to_f<T>(xs[t]);
     }
-    group_lse(m, s, g, red);  // barriers: every read of the stage is done
+    group_lse_wmax(m, s, g, red);  // barriers: every read of the stage is done
     if (abort_flag) break;
     pipe.refill();
     if (g.tx == 0) {
