@@ -312,15 +312,20 @@ __device__ __forceinline__ void group_lse_xwarp(float& m, float& s, const Group&
   __syncthreads();
 }
 
+// Within a warp (or a G < 32 group): the maximum by shuffles, each thread's
+// sum rescaled to it once, then a plain sum; one exponential per thread
+// instead of two per level of a pairwise merge.  Across warps: group_lse_xwarp.
 __device__ __forceinline__ void group_lse(float& m, float& s, const Group& g, float* red) {
   const int width = g.G < 32 ? g.G : 32;
+  float M = m;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)
-    if (o < width) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-      lse_merge(m, s, m2, s2);
-    }
+    if (o < width) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if (M != -INFINITY) s *= ex2_approx((m - M) * kLog2e);  // m = -inf: s is 0 and stays 0
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    if (o < width) s += __shfl_xor_sync(0xffffffffu, s, o);
+  m = M;
   if (g.G > 32) group_lse_xwarp(m, s, g, red);
 }
 
