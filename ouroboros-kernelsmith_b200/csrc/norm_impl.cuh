@@ -108,14 +108,25 @@ __device__ __forceinline__ void chan_merge(float& n, float& m, float& q, float n
 __device__ __forceinline__ void group_moments(float& n, float& m, float& q, const Group& g,
                                               float* red) {
   const int width = g.G < 32 ? g.G : 32;
+  // within a warp (or a G < 32 group): the count and the sum n*m by plain
+  // shuffle sums, the mean once, then the sum of q + n (m - mean)^2 -- the
+  // pairwise merge's result without its division per level
+  float nt = n, st = n * m;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)
     if (o < width) {
-      const float nb = __shfl_xor_sync(0xffffffffu, n, o);
-      const float mb = __shfl_xor_sync(0xffffffffu, m, o);
-      const float qb = __shfl_xor_sync(0xffffffffu, q, o);
-      chan_merge(n, m, q, nb, mb, qb);
+      nt += __shfl_xor_sync(0xffffffffu, nt, o);
+      st += __shfl_xor_sync(0xffffffffu, st, o);
     }
+  const float mt = nt > 0.0f ? st / nt : 0.0f;
+  const float d = m - mt;
+  float qt = fmaf(n * d, d, q);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    if (o < width) qt += __shfl_xor_sync(0xffffffffu, qt, o);
+  n = nt;
+  m = mt;
+  q = qt;
   if (g.G > 32) {
     // warp partials -> the group's first warp merges them with shuffles
     const int nw = g.G >> 5, w = g.tx >> 5, lane = g.tx & 31;
