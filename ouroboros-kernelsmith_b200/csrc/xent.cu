@@ -10,8 +10,11 @@
 //    S-stage shared-memory ring with bulk copies (full/empty mbarriers); the
 //    consumer warps fold each chunk into their running pairs and release the
 //    stage.  Loads never wait for the exponentials and vice versa.
+//  * ce_pipe_kernel (aligned rows of 4..64 KB, at most 8 rows per SM): whole
+//    rows through the block-wide row pipeline.
 //  * ce_rows_kernel (any layout): each thread walks its 16-byte vectors U at
-//    a time straight from global memory.  The target logit is a single scalar load; rows whose target is
+//    a time straight from global memory.
+// The target logit is a single scalar read; rows whose target is
 // ignore_index are not read at all.  b2k_ce_reduce sums per-row losses of a
 // shard in fp64 in a fixed order (deterministic) and counts valid rows;
 // b2k_ce_mean turns the (possibly all-reduced) pair into the mean.
