@@ -609,9 +609,14 @@ static int ce_launch(const CeArgs& a, cudaStream_t st, bool* bwd_done = nullptr)
   // faster (measured on the spec shape grid: 1024 x 4096 5.0 vs 7.2 us,
   // 8192 x 4096 21.2 vs 18.3 us).
   static const int use_pipe = ce_env("B2K_CE_PIPE", 1);
+  // B2K_CE_PIPE_RPS: most rows per SM that take the pipeline (default 8)
+  static const int pipe_rps = [] {
+    const int v = ce_env("B2K_CE_PIPE_RPS", 8);
+    return v >= 1 && v <= 1 << 20 ? v : 8;
+  }();
   const int64_t row_bytes = a.N * (int64_t)sizeof(T);
   if (use_tma && use_pipe && a.aligned && nvec >= 256 && row_bytes <= (64 << 10) &&
-      a.M <= 8 * (int64_t)sm_count()) {
+      a.M <= (int64_t)pipe_rps * sm_count()) {
     int G = next_pow2((nvec + 3) / 4);
     G = G < 64 ? 64 : (G > 512 ? 512 : G);
     const int64_t vneed = (nvec + G - 1) / G;
