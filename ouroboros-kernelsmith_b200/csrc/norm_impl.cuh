@@ -735,13 +735,15 @@ static bool norm_try_tma(const NormArgs& a, cudaStream_t st, int* status) {
   if (grid > a.M) grid = a.M;
   // LayerNorm statistics (B2K_LN_SHIFT: 0 Chan's merge, 2 shifted sums, 1 =
   // by shape): shifted sums, except when the residual stream is written and
-  // each block walks 12 rows or more, where Chan's merge measured faster
-  // (16384 x 8192 bf16 with h: 0.988 against 0.868 of the copy peak; 2048
-  // rows: 0.864 against 0.915; without h the shifted sums win at every shape,
+  // each block walks 8 rows or more, where Chan's merge measured faster
+  // (x + r -> LayerNorm -> GELU, 8192-wide bf16 rows with h, fractions of the
+  // copy peak, Chan against shifted: 16384 rows 0.977 / 0.87, 4096 rows
+  // 0.914 / 0.845, 3072 rows (10.4 per block) 0.881 / 0.871, 2048 rows (6.9
+  // per block) 0.854 / 0.926; without h the shifted sums win at every shape,
   // LayerNorm 8192 x 4096 bf16 0.81 against 0.64)
   NormArgs b = a;
   if (MODE == NM_LN && a.ln_shift == 1)
-    b.ln_shift = (a.h == nullptr || a.M < 12 * grid) ? 1 : 0;
+    b.ln_shift = (a.h == nullptr || a.M < 8 * grid) ? 1 : 0;
   launch_pdl(kern, (unsigned)grid, (unsigned)G, smem, st, b, S);
   *status = check_launch("b2k_norm(tma)");
   return true;
