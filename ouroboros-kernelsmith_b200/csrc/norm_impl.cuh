@@ -104,29 +104,47 @@ __device__ __forceinline__ void chan_merge(float& n, float& m, float& q, float n
   n = nt;
 }
 
+// Warp stage of the moments: bf16 kernels take plain shuffle sums (SUMS),
+// the others Chan's pairwise merge.  The sums (count, n*mean, then
+// q + n (mean - warp mean)^2) drop the division per level: the residual
+// LayerNorm at 16384 x 8192 bf16 0.1681 -> 0.1676 ms; in the fp16 and fp32
+// LayerNorm kernels, already at the 128-register cap, they made ptxas spill
+// and those kernels 5-7 % slower, so there the pairwise merge stays.
+template <typename T>
+constexpr bool kMomentSums = std::is_same<T, __nv_bfloat16>::value;
+
 // group-wide moments; `red` holds 1536 floats ([3][R<=16][32])
+template <bool SUMS>
 __device__ __forceinline__ void group_moments(float& n, float& m, float& q, const Group& g,
                                               float* red) {
   const int width = g.G < 32 ? g.G : 32;
-  // within a warp (or a G < 32 group): the count and the sum n*m by plain
-  // shuffle sums, the mean once, then the sum of q + n (m - mean)^2 -- the
-  // pairwise merge's result without its division per level
-  float nt = n, st = n * m;
+  if constexpr (SUMS) {
+    float nt = n, st = n * m;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-    if (o < width) {
-      nt += __shfl_xor_sync(0xffffffffu, nt, o);
-      st += __shfl_xor_sync(0xffffffffu, st, o);
-    }
-  const float mt = nt > 0.0f ? st / nt : 0.0f;
-  const float d = m - mt;
-  float qt = fmaf(n * d, d, q);
+    for (int o = 16; o > 0; o >>= 1)
+      if (o < width) {
+        nt += __shfl_xor_sync(0xffffffffu, nt, o);
+        st += __shfl_xor_sync(0xffffffffu, st, o);
+      }
+    const float mt = nt > 0.0f ? st / nt : 0.0f;
+    const float d = m - mt;
+    float qt = fmaf(n * d, d, q);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-    if (o < width) qt += __shfl_xor_sync(0xffffffffu, qt, o);
-  n = nt;
-  m = mt;
-  q = qt;
+    for (int o = 16; o > 0; o >>= 1)
+      if (o < width) qt += __shfl_xor_sync(0xffffffffu, qt, o);
+    n = nt;
+    m = mt;
+    q = qt;
+  } else {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+      if (o < width) {
+        const float nb = __shfl_xor_sync(0xffffffffu, n, o);
+        const float mb = __shfl_xor_sync(0xffffffffu, m, o);
+        const float qb = __shfl_xor_sync(0xffffffffu, q, o);
+        chan_merge(n, m, q, nb, mb, qb);
+      }
+  }
   if (g.G > 32) {
     // warp partials -> the group's first warp merges them with shuffles
     const int nw = g.G >> 5, w = g.tx >> 5, lane = g.tx & 31;
@@ -219,7 +237,7 @@ __device__ __forceinline__ void ln_stats_shift(const float2 (&hv)[V][H], int N, 
 // Statistics of a row slice held as pairs hv[V][H] (slot v covers elements
 // [(v*G+tx)*E, +E)); out-of-range elements hold 0.  `whole` = every slot is
 // either entirely inside or entirely outside the row (aligned rows).
-template <int MODE, int V, int H>
+template <int MODE, int V, int H, bool SUMS>
 __device__ __forceinline__ void row_stats(const float2 (&hv)[V][H], int N, bool whole,
                                           const Group& g, float* red, float eps, float& mu,
                                           float& rs) {
@@ -265,7 +283,7 @@ __device__ __forceinline__ void row_stats(const float2 (&hv)[V][H], int N, bool 
       }
     }
     float q = q2.x + q2.y;
-    group_moments(cnt, m, q, g, red);
+    group_moments<SUMS>(cnt, m, q, g, red);
     mu = m;
     rs = rsqrtf(q / (float)N + eps);
   } else {
@@ -341,7 +359,7 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_rows_kernel(const NormAr
   }
 
   float mu, rs;
-  row_stats<MODE, V, H>(hv, N, aligned, g, red, a.eps, mu, rs);
+  row_stats<MODE, V, H, kMomentSums<T>>(hv, N, aligned, g, red, a.eps, mu, rs);
   if (!valid) return;
 
   const float2 nmu2 = f2s(-mu), rs2 = f2s(rs);
@@ -508,7 +526,7 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_tma_kernel(const NormArg
     if (MODE == NM_LN && a.ln_shift) {
       ln_stats_shift<V, H>(hv, N, g, red, a.eps, K, mu, rs);
     } else {
-      row_stats<MODE, V, H>(hv, N, true, g, red, a.eps, mu, rs);
+      row_stats<MODE, V, H, kMomentSums<T>>(hv, N, true, g, red, a.eps, mu, rs);
     }
     // the reduction's barriers order every thread's reads of the stage
     // before the refill
@@ -605,7 +623,7 @@ __global__ void __launch_bounds__(kNormMaxThreads) norm_cluster_kernel(const Nor
         }
       }
     }
-    group_moments(cnt, m, q, g, red);
+    group_moments<kMomentSums<T>>(cnt, m, q, g, red);
     if (g.tx == 0) { part[0] = cnt; part[1] = m; part[2] = q; }
   } else {
     float2 q2 = f2s(0.0f);
