@@ -120,13 +120,18 @@ def run_rows_host(fn, row_inputs, other_inputs=(), *, out=None, chunk_rows=None,
                   device=None, n_slots=3, timing=None):
     """fn(*row_chunks, *other_inputs) -> Tensor or tuple of Tensors, applied to
     row chunks of `row_inputs` (host tensors with the same number of rows);
-    results are written into `out` (host tensors, allocated pinned if None).
-    Returns the tuple of host outputs (or the single output).  `timing`, a
+    results are written into `out` (host tensors, allocated pinned if None;
+    required when there are no rows).  Returns the tuple of host outputs (or
+    the single output).  `timing`, a
     pair of CUDA events, is recorded around all device work of the call."""
     device = torch.device(device or "cuda")
     # ~32 MB per operand per chunk: large enough to amortise the per-chunk
     # host work, small enough that the pipeline fills quickly
     rows, chunk_rows = _chunk_rows(row_inputs, chunk_rows, 32 << 20)
+    if rows == 0 and out is None:
+        # the outputs' shapes come from the op's first chunk; with no rows
+        # there is none
+        raise ValueError("b200k.host: zero rows need the host outputs (`out`)")
     cur = torch.cuda.current_stream(device)
     start = timing[0] if timing else torch.cuda.Event()
     start.record(cur)

@@ -17,6 +17,11 @@ def test_chunk_rows_checks_the_row_inputs():
         _chunk_rows([torch.zeros(10, 4)], 0, 64)
 
 
+def test_zero_rows_need_host_outputs():
+    with pytest.raises(ValueError):
+        run_rows_host(lambda x: x, [torch.zeros(0, 4)])
+
+
 def test_captured_pipeline_takes_pinned_buffers_only():
     t = torch.zeros(3, 4)
     with pytest.raises(ValueError):
